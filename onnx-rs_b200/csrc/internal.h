@@ -1,0 +1,94 @@
+// Host-side internals shared by api.cpp and graph.cpp.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+#include <vector>
+
+#include "../../include/onnxb200.h"
+#include "kernels.h"
+
+struct onnxb200_handle {
+  int device = 0;
+  int num_sms = 148;
+  cudaStream_t own_stream = nullptr;
+  cudaStream_t stream = nullptr;
+  onnxb200_options opts{};
+  void* ws = nullptr;        // workspace (grows on demand, stream-ordered reuse)
+  size_t ws_bytes = 0;
+  int* d_status = nullptr;   // device status word written by kernels
+  float* d_ones = nullptr;   // scratch constants
+  std::string last_error;
+  int64_t launches = 0;
+};
+
+struct onnxb200_conv_plan {
+  onnxb200_conv_desc d{};    // pads resolved, precision resolved
+  int64_t oh = 0, ow = 0;
+  int prec = 0;
+  bool use_tc = false;       // tcgen05 implicit GEMM (else CUDA-core direct conv)
+  int cs_in = 0;             // channel stride of the NHWC input the plan expects
+  int K = 0, num_kb = 0, kpad = 0, bn = 128;
+  void* w_hi = nullptr;      // packed weights (tc path)
+  void* w_lo = nullptr;
+  float* w_oihw = nullptr;   // original weights (CUDA-core path)
+  float* scale = nullptr;    // epilogue per-channel multiplier (BN) or null
+  float* shift = nullptr;    // epilogue per-channel addend (bias / BN) or null
+  CUtensorMap tm_hi{}, tm_lo{};
+  int64_t weight_bytes = 0;
+};
+
+namespace ob2 {
+
+int set_error(onnxb200_handle* h, int code, const std::string& msg);
+int cuda_check(onnxb200_handle* h, cudaError_t e, const char* what);
+int ensure_workspace(onnxb200_handle* h, size_t bytes);
+
+// Encodes a 2-D TMA map over a [rows][kpad] K-major weight matrix.
+int encode_weight_map(onnxb200_handle* h, CUtensorMap* map, const void* base, int rows, int kpad,
+                      int prec, int bn);
+
+// Resolves auto_pad / defaults and validates a conv descriptor.
+int resolve_conv_desc(onnxb200_handle* h, const onnxb200_conv_desc* in, onnxb200_conv_desc* out,
+                      int64_t* oh, int64_t* ow);
+
+// Builds a conv plan whose weights live in memory owned by the plan (cudaMalloc)
+// or, when `scratch` is non-null, inside the given scratch region (no allocation).
+// With scratch == nullptr and scratch_used != nullptr it only reports the bytes
+// the plan needs.
+int conv_plan_init(onnxb200_handle* h, const onnxb200_conv_desc* d, int cs_in, const float* w,
+                   const float* bias, const float* bn_scale, const float* bn_bias,
+                   const float* bn_mean, const float* bn_var, onnxb200_conv_plan* p,
+                   void* scratch, size_t scratch_bytes, size_t* scratch_used);
+void conv_plan_free(onnxb200_conv_plan* p);
+
+// Runs a plan on NHWC buffers (x channel stride p->cs_in, y / residual stride C_out).
+int conv_plan_exec_nhwc(onnxb200_handle* h, const onnxb200_conv_plan* p, const float* x,
+                        const float* residual, float* y);
+
+// Plain GEMM on the tcgen05 core:  y[b] = A_b * B_b^T(packed) with epilogue.
+struct GemmCall {
+  const float* a = nullptr;  // row-major [M][K] per batch, lda == K
+  int M = 0, N = 0, K = 0;
+  int batches = 1;
+  const long long* a_off = nullptr;  // device array or null
+  const int* b_row = nullptr;        // device array or null
+  long long y_bstride = 0;
+  float* y = nullptr;
+  int ldy = 0;
+  const float* scale = nullptr;
+  const float* shift = nullptr;
+  const float* res = nullptr;
+  int ldr = 0;
+  int relu = 0;
+};
+int gemm_tc_run(onnxb200_handle* h, const GemmCall& c, const void* b_hi, const void* b_lo,
+                int b_rows, int kpad, int prec);
+
+inline int resolve_prec(const onnxb200_handle* h, int prec) {
+  return prec < 0 ? h->opts.precision : prec;
+}
+
+}  // namespace ob2

@@ -1,0 +1,106 @@
+// Device-kernel launch interface shared by the C-ABI layer and the kernels.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace ob2 {
+
+enum Precision { kPrec3xTF32 = 0, kPrecTF32 = 1, kPrecBF16 = 2, kPrecFP32 = 3 };
+
+// Implicit-GEMM problem: D[b][m][n] = sum_k A_b[m][k] * B_b[n][k], then the
+// epilogue  y = D * scale[n] + shift[n] (+ residual) (relu).
+//   A rows are output pixels of a convolution over an NHWC input (a plain
+//   row-major matrix is the 1x1 / stride-1 / H=1 special case); K is ordered
+//   (kh, kw, c) with c fastest, c padded to `Cs` channels per pixel.
+//   B is the packed weight matrix [rows][Kpad] (K-major), read through TMA.
+struct IgemmParams {
+  const float* x;      // NHWC activations (or row-major A)
+  int Hin, Win, Cs;    // input height, width, channels per pixel (multiple of 4)
+  int OH, OW;          // output height, width
+  int KW;              // filter width
+  int sh, sw, ph, pw, dh, dw;
+  int M;               // rows per batch = N*OH*OW (or matrix M)
+  int Nc;              // columns (output channels / matrix N), multiple of 4
+  int K;               // KH*KW*Cs (real K)
+  int num_kb;          // ceil(K / 32)
+  int batches;         // independent GEMMs (MatMul batch); 1 for conv
+  const long long* a_off;  // per-batch element offset into x (nullptr = 0)
+  const int* b_row;        // per-batch row offset into B (nullptr = 0)
+  long long y_bstride;     // per-batch element stride of y / residual
+  float* y;
+  int ldy;                 // row stride of y in elements
+  const float* scale;      // per-column multiplier (nullptr = 1)
+  const float* shift;      // per-column addend (nullptr = 0)
+  const float* res;        // residual, same layout as y (nullptr = none)
+  int ldr;
+  int relu;
+  int* status;             // device status word (ONNXB200_ERR_* on failure)
+  int m_tiles, n_tiles;
+};
+
+// Picks BN (64/128/256) for a problem; returned value is what launch uses.
+int igemm_pick_bn(const IgemmParams& p, int precision, int num_sms);
+
+// Launches the tcgen05 kernel.  tm_hi / tm_lo are TMA maps over the packed
+// weights (tm_lo is only read in 3xTF32 mode).  Returns a cudaError_t.
+int igemm_launch(const IgemmParams& p, const CUtensorMap& tm_hi, const CUtensorMap& tm_lo,
+                 int precision, int bn, int num_sms, cudaStream_t stream);
+
+// ----------------------------------------------------------------- SIMT kernels
+// Direct convolution on CUDA cores (fp32 FFMA), any groups / channel count.
+// NHWC in, NHWC out, weights OIHW (original layout), same epilogue.
+int conv_direct_launch(const float* x, int N, int H, int W, int C, int Cs, const float* w,
+                       int CO, int KH, int KW, int sh, int sw, int ph, int pw, int dh, int dw, int group,
+                       int OH, int OW, const float* scale, const float* shift, const float* res,
+                       int relu, float* y, cudaStream_t stream);
+
+// Plain batched GEMM on CUDA cores for shapes the tcgen05 kernel does not take.
+// C[b] = alpha * op(A[b]) * op(B[b]) ; epilogue as above.
+int gemm_simt_launch(const float* a, const float* b, int batches, const long long* a_off,
+                     const long long* b_off, long long y_bstride, int M, int N, int K, int lda,
+                     int ldb, int trans_a, int trans_b, const float* scale, const float* shift,
+                     const float* res, int ldr, int relu, float* y, int ldy, cudaStream_t stream);
+
+// Packs fp32 weights into the K-major [rows][Kpad] operand of the tcgen05
+// kernel.  src element (row, k) is read from
+//   src[(row/rpg)*gs + (row%rpg)*rs + (k/Cs)*ts + (k%Cs)*cs]
+// for k%Cs < Creal, zero otherwise (and zero for k >= K).  For 3xTF32 both hi
+// and lo are written; for TF32 only hi; for BF16 `hi` receives bf16 values.
+int pack_b_launch(const float* src, int rows, int K, int Kpad, int Cs, int Creal, int rpg,
+                  long long gs, long long rs, long long ts, long long cs, int precision,
+                  void* hi, void* lo, cudaStream_t stream);
+
+// NCHW -> NHWC with channel padding to Cp (zero-filled), and NHWC -> NCHW.
+int nchw_to_nhwc_launch(const float* x, int N, int C, int H, int W, int Cp, float* y,
+                        cudaStream_t stream);
+int nhwc_to_nchw_launch(const float* x, int N, int C, int H, int W, int Cs, float* y,
+                        cudaStream_t stream);
+
+// MaxPool 2-D over NHWC (channel stride Cs), optional int64 NCHW flat indices.
+int maxpool_nhwc_launch(const float* x, int N, int C, int Cs, int H, int W, int KH, int KW,
+                        int sh, int sw, int pt, int pl, int OH, int OW, float* y,
+                        long long* indices, cudaStream_t stream);
+
+// Global average pool over NHWC: y[n][c] = mean over H*W.
+int gap_nhwc_launch(const float* x, int N, int C, int HW, float* y, cudaStream_t stream);
+
+// Broadcast binary add (rank <= 8) with optional relu; and relu alone.
+int add_broadcast_launch(const float* a, const float* b, float* y, int rank,
+                         const long long* out_shape, const long long* a_strides,
+                         const long long* b_strides, long long total, int relu,
+                         cudaStream_t stream);
+int relu_launch(const float* x, float* y, long long n, cudaStream_t stream);
+
+// Per-channel affine (BatchNormalization as scale/shift) over NHWC or NCHW.
+int channel_affine_launch(const float* x, const float* scale, const float* shift, float* y,
+                          long long outer, int C, long long inner, int relu,
+                          cudaStream_t stream);
+
+// Computes scale = gamma / sqrt(var + eps), shift = beta + (bias - mean) * scale
+// (bias may be null) on the device.
+int bn_fold_launch(const float* gamma, const float* beta, const float* mean, const float* var,
+                   const float* bias, float eps, int C, float* scale, float* shift,
+                   cudaStream_t stream);
+
+}  // namespace ob2

@@ -1,0 +1,506 @@
+// CUDA-core kernels of the path: grouped / general direct convolution, a
+// fallback batched GEMM, weight packing for the tcgen05 kernel, layout
+// repacks, MaxPool, GlobalAveragePool and elementwise ops.  All memory-bound
+// kernels move 16-byte vectors along the channel (innermost NHWC) axis.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "kernels.h"
+#include "ptx.cuh"
+
+namespace ob2 {
+
+namespace {
+constexpr int kBlock = 256;
+
+inline int grid_for(long long n, int block) {
+  long long g = (n + block - 1) / block;
+  if (g > (1ll << 30)) g = 1ll << 30;
+  return (int)(g < 1 ? 1 : g);
+}
+
+__device__ __forceinline__ float epi(float v, const float* scale, const float* shift, int c) {
+  if (scale) v *= scale[c];
+  if (shift) v += shift[c];
+  return v;
+}
+}  // namespace
+
+// ------------------------------------------------------------------ direct conv
+// compute_conv2d_direct_impl (src/ops/nn/conv.rs:849-935) on NHWC data: one
+// thread per output element (n, oh, ow, co) with co fastest; sums over
+// (ci, kh, kw) of its group in fp32.
+__global__ void conv_direct_kernel(const float* __restrict__ x, int N, int H, int W, int C,
+                                   int Cs, const float* __restrict__ w, int CO, int KH, int KW, int sh,
+                                   int sw, int ph, int pw, int dh, int dw, int group, int OH,
+                                   int OW, const float* __restrict__ scale,
+                                   const float* __restrict__ shift, const float* __restrict__ res,
+                                   int relu, float* __restrict__ y) {
+  const long long total = (long long)N * OH * OW * CO;
+  const int cg = C / group, cog = CO / group;
+  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int co = (int)(idx % CO);
+    long long pix = idx / CO;
+    const int ow = (int)(pix % OW);
+    const int oh = (int)((pix / OW) % OH);
+    const int n = (int)(pix / ((long long)OW * OH));
+    const int g = co / cog;
+    float sum = 0.f;
+    for (int ci = 0; ci < cg; ++ci) {
+      const float* wp = w + ((long long)co * cg + ci) * KH * KW;
+      for (int r = 0; r < KH; ++r) {
+        const int ih = oh * sh - ph + r * dh;
+        if ((unsigned)ih >= (unsigned)H) continue;
+        for (int s = 0; s < KW; ++s) {
+          const int iw = ow * sw - pw + s * dw;
+          if ((unsigned)iw >= (unsigned)W) continue;
+          sum = fmaf(x[(((long long)n * H + ih) * W + iw) * Cs + g * cg + ci], wp[r * KW + s], sum);
+        }
+      }
+    }
+    float v = epi(sum, scale, shift, co);
+    if (res) v += res[idx];
+    if (relu) v = v > 0.f ? v : 0.f;
+    y[idx] = v;
+  }
+}
+
+int conv_direct_launch(const float* x, int N, int H, int W, int C, int Cs, const float* w, int CO,
+                       int KH, int KW, int sh, int sw, int ph, int pw, int dh, int dw, int group, int OH,
+                       int OW, const float* scale, const float* shift, const float* res, int relu,
+                       float* y, cudaStream_t st) {
+  const long long total = (long long)N * OH * OW * CO;
+  if (total == 0) return 0;
+  conv_direct_kernel<<<grid_for(total, kBlock), kBlock, 0, st>>>(
+      x, N, H, W, C, Cs, w, CO, KH, KW, sh, sw, ph, pw, dh, dw, group, OH, OW, scale, shift, res,
+      relu, y);
+  return (int)cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ SIMT GEMM
+// 64x64 tile, 256 threads, 4x4 outputs per thread, fp32 FFMA.
+__global__ void gemm_simt_kernel(const float* __restrict__ a, const float* __restrict__ b,
+                                 const long long* a_off, const long long* b_off,
+                                 long long y_bstride, int M, int N, int K, int lda, int ldb,
+                                 int ta, int tb, const float* __restrict__ scale,
+                                 const float* __restrict__ shift, const float* __restrict__ res,
+                                 int ldr, int relu, float* __restrict__ y, int ldy) {
+  __shared__ float As[16][64 + 1];
+  __shared__ float Bs[16][64 + 1];
+  const int bz = blockIdx.z;
+  const float* A = a + (a_off ? a_off[bz] : 0);
+  const float* B = b + (b_off ? b_off[bz] : 0);
+  float* Y = y + (long long)bz * y_bstride;
+  const float* R = res ? res + (long long)bz * y_bstride : nullptr;
+  const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < K; k0 += 16) {
+    for (int i = threadIdx.x; i < 16 * 64; i += 256) {
+      const int kk = i / 64, mm = i % 64;
+      const int gm = m0 + mm, gk = k0 + kk;
+      float v = 0.f;
+      if (gm < M && gk < K) v = ta ? A[(long long)gk * lda + gm] : A[(long long)gm * lda + gk];
+      As[kk][mm] = v;
+      const int gn = n0 + mm;
+      float u = 0.f;
+      if (gn < N && gk < K) u = tb ? B[(long long)gn * ldb + gk] : B[(long long)gk * ldb + gn];
+      Bs[kk][mm] = u;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < 16; ++kk) {
+      float av[4], bv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) av[i] = As[kk][ty * 4 + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) bv[j] = Bs[kk][tx * 4 + j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int gm = m0 + ty * 4 + i;
+    if (gm >= M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int gn = n0 + tx * 4 + j;
+      if (gn >= N) continue;
+      float v = epi(acc[i][j], scale, shift, gn);
+      if (R) v += R[(long long)gm * ldr + gn];
+      if (relu) v = v > 0.f ? v : 0.f;
+      Y[(long long)gm * ldy + gn] = v;
+    }
+  }
+}
+
+int gemm_simt_launch(const float* a, const float* b, int batches, const long long* a_off,
+                     const long long* b_off, long long y_bstride, int M, int N, int K, int lda,
+                     int ldb, int ta, int tb, const float* scale, const float* shift,
+                     const float* res, int ldr, int relu, float* y, int ldy, cudaStream_t st) {
+  if (M == 0 || N == 0 || batches == 0) return 0;
+  dim3 grid((N + 63) / 64, (M + 63) / 64, batches);
+  gemm_simt_kernel<<<grid, 256, 0, st>>>(a, b, a_off, b_off, y_bstride, M, N, K, lda, ldb, ta, tb,
+                                          scale, shift, res, ldr, relu, y, ldy);
+  return (int)cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ weight packing
+__global__ void pack_b_kernel(const float* __restrict__ src, int rows, int K, int Kpad, int Cs,
+                              int Creal, int rpg, long long gs, long long rs, long long ts,
+                              long long cs, int prec, void* hi, void* lo) {
+  const long long total = (long long)rows * Kpad;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int row = (int)(i / Kpad);
+    const int k = (int)(i % Kpad);
+    float v = 0.f;
+    if (k < K) {
+      const int tap = k / Cs, c = k % Cs;
+      if (c < Creal) v = src[(long long)(row / rpg) * gs + (long long)(row % rpg) * rs + tap * ts + c * cs];
+    }
+    if (prec == kPrecBF16) {
+      reinterpret_cast<__nv_bfloat16*>(hi)[i] = __float2bfloat16_rn(v);
+    } else if (prec == kPrecFP32) {
+      reinterpret_cast<float*>(hi)[i] = v;
+    } else {
+      const float h = to_tf32(v);
+      reinterpret_cast<float*>(hi)[i] = h;
+      if (prec == kPrec3xTF32) reinterpret_cast<float*>(lo)[i] = to_tf32(v - h);
+    }
+  }
+}
+
+int pack_b_launch(const float* src, int rows, int K, int Kpad, int Cs, int Creal, int rpg,
+                  long long gs, long long rs, long long ts, long long cs, int prec, void* hi,
+                  void* lo, cudaStream_t st) {
+  const long long total = (long long)rows * Kpad;
+  if (total == 0) return 0;
+  pack_b_kernel<<<grid_for(total, kBlock), kBlock, 0, st>>>(src, rows, K, Kpad, Cs, Creal, rpg,
+                                                            gs, rs, ts, cs, prec, hi, lo);
+  return (int)cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ layout repacks
+// 32x32 tiles through shared memory: NCHW [n][c][hw] <-> NHWC [n][hw][c].
+__global__ void nchw_to_nhwc_kernel(const float* __restrict__ x, int C, int HW, int Cp,
+                                    float* __restrict__ y) {
+  __shared__ float t[32][33];
+  const int n = blockIdx.z;
+  const int hw0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
+  const float* xn = x + (long long)n * C * HW;
+  float* yn = y + (long long)n * HW * Cp;
+  for (int j = threadIdx.y; j < 32; j += 8) {
+    const int c = c0 + j, hw = hw0 + threadIdx.x;
+    t[j][threadIdx.x] = (c < C && hw < HW) ? xn[(long long)c * HW + hw] : 0.f;
+  }
+  __syncthreads();
+  for (int j = threadIdx.y; j < 32; j += 8) {
+    const int hw = hw0 + j, c = c0 + threadIdx.x;
+    if (hw < HW && c < Cp) yn[(long long)hw * Cp + c] = t[threadIdx.x][j];
+  }
+}
+
+int nchw_to_nhwc_launch(const float* x, int N, int C, int H, int W, int Cp, float* y,
+                        cudaStream_t st) {
+  const int HW = H * W;
+  if ((long long)N * HW * Cp == 0) return 0;
+  dim3 grid((HW + 31) / 32, (Cp + 31) / 32, N);
+  nchw_to_nhwc_kernel<<<grid, dim3(32, 8), 0, st>>>(x, C, HW, Cp, y);
+  return (int)cudaGetLastError();
+}
+
+__global__ void nhwc_to_nchw_kernel(const float* __restrict__ x, int C, int HW, int Cs,
+                                    float* __restrict__ y) {
+  __shared__ float t[32][33];
+  const int n = blockIdx.z;
+  const int hw0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
+  const float* xn = x + (long long)n * HW * Cs;
+  float* yn = y + (long long)n * C * HW;
+  for (int j = threadIdx.y; j < 32; j += 8) {
+    const int hw = hw0 + j, c = c0 + threadIdx.x;
+    t[j][threadIdx.x] = (hw < HW && c < C) ? xn[(long long)hw * Cs + c] : 0.f;
+  }
+  __syncthreads();
+  for (int j = threadIdx.y; j < 32; j += 8) {
+    const int c = c0 + j, hw = hw0 + threadIdx.x;
+    if (c < C && hw < HW) yn[(long long)c * HW + hw] = t[threadIdx.x][j];
+  }
+}
+
+int nhwc_to_nchw_launch(const float* x, int N, int C, int H, int W, int Cs, float* y,
+                        cudaStream_t st) {
+  const int HW = H * W;
+  if ((long long)N * HW * C == 0) return 0;
+  dim3 grid((HW + 31) / 32, (C + 31) / 32, N);
+  nhwc_to_nchw_kernel<<<grid, dim3(32, 8), 0, st>>>(x, C, HW, Cs, y);
+  return (int)cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ MaxPool
+// max_pool (src/ops/nn/pool.rs:307-393): init f32::MIN, in-bounds taps only,
+// fmaxf ignores NaN like f32::max.  Vector path: one thread per (pixel, 4 channels).
+__global__ void maxpool_nhwc_v4_kernel(const float* __restrict__ x, int N, int C4, int Cs, int H,
+                                       int W, int KH, int KW, int sh, int sw, int pt, int pl,
+                                       int OH, int OW, float* __restrict__ y) {
+  const long long total = (long long)N * OH * OW * C4;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int c4 = (int)(i % C4);
+    const long long pix = i / C4;
+    const int ow = (int)(pix % OW);
+    const int oh = (int)((pix / OW) % OH);
+    const int n = (int)(pix / ((long long)OW * OH));
+    float4 m = make_float4(-3.40282347e+38f, -3.40282347e+38f, -3.40282347e+38f, -3.40282347e+38f);
+    for (int r = 0; r < KH; ++r) {
+      const int ih = oh * sh - pt + r;
+      if ((unsigned)ih >= (unsigned)H) continue;
+      for (int s = 0; s < KW; ++s) {
+        const int iw = ow * sw - pl + s;
+        if ((unsigned)iw >= (unsigned)W) continue;
+        const float4 v =
+            *reinterpret_cast<const float4*>(x + (((long long)n * H + ih) * W + iw) * Cs + 4 * c4);
+        m.x = fmaxf(m.x, v.x);
+        m.y = fmaxf(m.y, v.y);
+        m.z = fmaxf(m.z, v.z);
+        m.w = fmaxf(m.w, v.w);
+      }
+    }
+    *reinterpret_cast<float4*>(y + pix * (long long)Cs + 4 * c4) = m;
+  }
+}
+
+// Scalar path with indices: the ONNX flat NCHW index of the first maximum.
+__global__ void maxpool_nhwc_idx_kernel(const float* __restrict__ x, int N, int C, int Cs, int H,
+                                        int W, int KH, int KW, int sh, int sw, int pt, int pl,
+                                        int OH, int OW, float* __restrict__ y,
+                                        long long* __restrict__ ind) {
+  const long long total = (long long)N * OH * OW * C;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int c = (int)(i % C);
+    const long long pix = i / C;
+    const int ow = (int)(pix % OW);
+    const int oh = (int)((pix / OW) % OH);
+    const int n = (int)(pix / ((long long)OW * OH));
+    float m = -3.40282347e+38f;
+    long long mi = -1;
+    for (int r = 0; r < KH; ++r) {
+      const int ih = oh * sh - pt + r;
+      if ((unsigned)ih >= (unsigned)H) continue;
+      for (int s = 0; s < KW; ++s) {
+        const int iw = ow * sw - pl + s;
+        if ((unsigned)iw >= (unsigned)W) continue;
+        const float v = x[(((long long)n * H + ih) * W + iw) * Cs + c];
+        if (v > m || (mi < 0 && v == m)) {
+          m = v;
+          mi = (((long long)n * C + c) * H + ih) * W + iw;
+        }
+      }
+    }
+    y[pix * Cs + c] = m;
+    if (ind) ind[(((long long)n * C + c) * OH + oh) * OW + ow] = mi;
+  }
+}
+
+int maxpool_nhwc_launch(const float* x, int N, int C, int Cs, int H, int W, int KH, int KW, int sh,
+                        int sw, int pt, int pl, int OH, int OW, float* y, long long* ind,
+                        cudaStream_t st) {
+  if (!ind && C % 4 == 0 && Cs % 4 == 0) {
+    const long long total = (long long)N * OH * OW * (C / 4);
+    if (total == 0) return 0;
+    maxpool_nhwc_v4_kernel<<<grid_for(total, kBlock), kBlock, 0, st>>>(
+        x, N, C / 4, Cs, H, W, KH, KW, sh, sw, pt, pl, OH, OW, y);
+  } else {
+    const long long total = (long long)N * OH * OW * C;
+    if (total == 0) return 0;
+    maxpool_nhwc_idx_kernel<<<grid_for(total, kBlock), kBlock, 0, st>>>(
+        x, N, C, Cs, H, W, KH, KW, sh, sw, pt, pl, OH, OW, y, ind);
+  }
+  return (int)cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ GlobalAveragePool
+// global_pool (src/ops/nn/pool.rs:493-557): each thread sums its channel over
+// H*W sequentially in fp32 (the reference's order) and divides by the count.
+__global__ void gap_nhwc_kernel(const float* __restrict__ x, int C, int HW,
+                                float* __restrict__ y) {
+  const int n = blockIdx.y;
+  const int c4 = blockIdx.x * blockDim.x + threadIdx.x;
+  if (4 * c4 >= C) return;
+  const float* p = x + (long long)n * HW * C + 4 * c4;
+  float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int i = 0; i < HW; ++i) {
+    const float4 v = *reinterpret_cast<const float4*>(p + (long long)i * C);
+    s.x += v.x;
+    s.y += v.y;
+    s.z += v.z;
+    s.w += v.w;
+  }
+  const float cnt = (float)HW;
+  *reinterpret_cast<float4*>(y + (long long)n * C + 4 * c4) =
+      make_float4(s.x / cnt, s.y / cnt, s.z / cnt, s.w / cnt);
+}
+
+__global__ void gap_nhwc_scalar_kernel(const float* __restrict__ x, int C, int HW,
+                                       float* __restrict__ y) {
+  const int n = blockIdx.y;
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  const float* p = x + (long long)n * HW * C + c;
+  float s = 0.f;
+  for (int i = 0; i < HW; ++i) s += p[(long long)i * C];
+  y[(long long)n * C + c] = s / (float)HW;
+}
+
+int gap_nhwc_launch(const float* x, int N, int C, int HW, float* y, cudaStream_t st) {
+  if (N == 0 || C == 0) return 0;
+  if (C % 4 == 0) {
+    const int c4 = C / 4;
+    const int block = c4 < 128 ? 32 * ((c4 + 31) / 32) : 128;
+    dim3 grid((c4 + block - 1) / block, N);
+    gap_nhwc_kernel<<<grid, block, 0, st>>>(x, C, HW, y);
+  } else {
+    dim3 grid((C + 127) / 128, N);
+    gap_nhwc_scalar_kernel<<<grid, 128, 0, st>>>(x, C, HW, y);
+  }
+  return (int)cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ elementwise
+struct BcastArgs {
+  long long shape[8];
+  long long as[8];
+  long long bs[8];
+};
+
+// element_wise_binary_op(+) (src/ops/tensor.rs:1124-1218) without materialising
+// the broadcast copies: stride 0 on broadcast dims.
+__global__ void add_bcast_kernel(const float* __restrict__ a, const float* __restrict__ b,
+                                 float* __restrict__ y, int rank, BcastArgs g, long long total,
+                                 int relu) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    long long rem = i, ia = 0, ib = 0;
+    for (int d = rank - 1; d >= 0; --d) {
+      const long long c = rem % g.shape[d];
+      rem /= g.shape[d];
+      ia += c * g.as[d];
+      ib += c * g.bs[d];
+    }
+    float v = a[ia] + b[ib];
+    if (relu) v = v > 0.f ? v : 0.f;
+    y[i] = v;
+  }
+}
+
+__global__ void add_same_v4_kernel(const float4* __restrict__ a, const float4* __restrict__ b,
+                                   float4* __restrict__ y, long long n4, int relu) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4;
+       i += (long long)gridDim.x * blockDim.x) {
+    const float4 u = a[i], v = b[i];
+    float4 r = make_float4(u.x + v.x, u.y + v.y, u.z + v.z, u.w + v.w);
+    if (relu) {
+      r.x = r.x > 0.f ? r.x : 0.f;
+      r.y = r.y > 0.f ? r.y : 0.f;
+      r.z = r.z > 0.f ? r.z : 0.f;
+      r.w = r.w > 0.f ? r.w : 0.f;
+    }
+    y[i] = r;
+  }
+}
+
+int add_broadcast_launch(const float* a, const float* b, float* y, int rank,
+                         const long long* shape, const long long* as, const long long* bs,
+                         long long total, int relu, cudaStream_t st) {
+  if (total == 0) return 0;
+  bool same = true;
+  long long expect = 1;
+  for (int d = rank - 1; d >= 0; --d) {
+    if (shape[d] != 1 && (as[d] != expect || bs[d] != expect)) same = false;
+    expect *= shape[d];
+  }
+  const bool aligned = ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
+                         reinterpret_cast<uintptr_t>(y)) & 15) == 0;
+  if (same && total % 4 == 0 && aligned) {
+    add_same_v4_kernel<<<grid_for(total / 4, kBlock), kBlock, 0, st>>>(
+        reinterpret_cast<const float4*>(a), reinterpret_cast<const float4*>(b),
+        reinterpret_cast<float4*>(y), total / 4, relu);
+  } else {
+    BcastArgs g{};
+    for (int d = 0; d < rank; ++d) {
+      g.shape[d] = shape[d];
+      g.as[d] = as[d];
+      g.bs[d] = bs[d];
+    }
+    add_bcast_kernel<<<grid_for(total, kBlock), kBlock, 0, st>>>(a, b, y, rank, g, total, relu);
+  }
+  return (int)cudaGetLastError();
+}
+
+// relu (src/ops/activations.rs:244-246): v > 0 ? v : 0 (NaN -> 0).
+__global__ void relu_kernel(const float* __restrict__ x, float* __restrict__ y, long long n) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const float v = x[i];
+    y[i] = v > 0.f ? v : 0.f;
+  }
+}
+
+int relu_launch(const float* x, float* y, long long n, cudaStream_t st) {
+  if (n == 0) return 0;
+  relu_kernel<<<grid_for(n, kBlock), kBlock, 0, st>>>(x, y, n);
+  return (int)cudaGetLastError();
+}
+
+// y = x * scale[c] + shift[c] over [outer][C][inner] (NCHW: inner = H*W;
+// NHWC: outer = N*H*W, inner = 1).
+__global__ void channel_affine_kernel(const float* __restrict__ x, const float* __restrict__ scale,
+                                      const float* __restrict__ shift, float* __restrict__ y,
+                                      long long outer, int C, long long inner, int relu) {
+  const long long total = outer * C * inner;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int c = (int)((i / inner) % C);
+    float v = x[i] * scale[c] + shift[c];
+    if (relu) v = v > 0.f ? v : 0.f;
+    y[i] = v;
+  }
+}
+
+int channel_affine_launch(const float* x, const float* scale, const float* shift, float* y,
+                          long long outer, int C, long long inner, int relu, cudaStream_t st) {
+  const long long total = outer * C * inner;
+  if (total == 0) return 0;
+  channel_affine_kernel<<<grid_for(total, kBlock), kBlock, 0, st>>>(x, scale, shift, y, outer, C,
+                                                                    inner, relu);
+  return (int)cudaGetLastError();
+}
+
+// BatchNormalization folded to a per-channel affine of the conv accumulator.
+__global__ void bn_fold_kernel(const float* gamma, const float* beta, const float* mean,
+                               const float* var, const float* bias, float eps, int C,
+                               float* scale, float* shift) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  const float s = gamma[c] / sqrtf(var[c] + eps);
+  const float b = bias ? bias[c] : 0.f;
+  scale[c] = s;
+  shift[c] = beta[c] + (b - mean[c]) * s;
+}
+
+int bn_fold_launch(const float* gamma, const float* beta, const float* mean, const float* var,
+                   const float* bias, float eps, int C, float* scale, float* shift,
+                   cudaStream_t st) {
+  if (C == 0) return 0;
+  bn_fold_kernel<<<(C + 127) / 128, 128, 0, st>>>(gamma, beta, mean, var, bias, eps, C, scale,
+                                                  shift);
+  return (int)cudaGetLastError();
+}
+
+}  // namespace ob2

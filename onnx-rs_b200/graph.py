@@ -1,0 +1,166 @@
+"""Graph API: the ExecutionEngine (src/execution/engine.rs:75-231) of this path.
+
+``Graph(handle, nodes, initializers, inputs, outputs)`` hands an ONNX-style node
+list to ``onnxb200_graph_build`` (fusion, NHWC weight packing, one activation
+arena, CUDA-graph capture on replay) and runs it on device or host buffers.
+Nodes use the same dict form as the oracle: ``{"op", "inputs", "outputs", "attrs"}``.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Dict, List, Sequence, Tuple
+
+import numpy as np
+import torch
+
+from . import _capi as C
+from .runtime import Handle, dptr
+
+
+def _c_node(nd: dict, keep: list) -> C.Node:
+    ins = [s.encode() if s else b"" for s in nd["inputs"]]
+    outs = [s.encode() for s in nd["outputs"]]
+    in_arr = (ctypes.c_char_p * max(1, len(ins)))(*ins)
+    out_arr = (ctypes.c_char_p * max(1, len(outs)))(*outs)
+    attrs = []
+    for k, v in nd.get("attrs", {}).items():
+        a = C.Attr()
+        a.name = k.encode()
+        keep.append(a.name)
+        if isinstance(v, str):
+            a.type = C.ATTR_STRING
+            a.s = v.encode()
+            keep.append(a.s)
+        elif isinstance(v, float):
+            a.type = C.ATTR_FLOAT
+            a.f = v
+        elif isinstance(v, (list, tuple)):
+            a.type = C.ATTR_INTS
+            arr = C.i64_array(v)
+            keep.append(arr)
+            a.ints = ctypes.cast(arr, ctypes.POINTER(ctypes.c_int64))
+            a.n_ints = len(v)
+        else:
+            a.type = C.ATTR_INT
+            a.i = int(v)
+        attrs.append(a)
+    attr_arr = (C.Attr * max(1, len(attrs)))(*attrs)
+    keep += [ins, outs, in_arr, out_arr, attr_arr]
+    n = C.Node()
+    n.op_type = nd["op"].encode()
+    keep.append(n.op_type)
+    n.inputs = ctypes.cast(in_arr, ctypes.POINTER(ctypes.c_char_p))
+    n.n_inputs = len(ins)
+    n.outputs = ctypes.cast(out_arr, ctypes.POINTER(ctypes.c_char_p))
+    n.n_outputs = len(outs)
+    n.attrs = ctypes.cast(attr_arr, ctypes.POINTER(C.Attr))
+    n.n_attrs = len(attrs)
+    return n
+
+
+class Graph:
+    def __init__(self, handle: Handle, nodes: Sequence[dict], initializers: Dict[str, np.ndarray],
+                 inputs: Sequence[Tuple[str, Sequence[int]]], outputs: Sequence[str]):
+        self.handle = handle
+        self.input_specs = [(n, list(s)) for n, s in inputs]
+        self.output_names = list(outputs)
+        keep: list = []
+        cnodes = (C.Node * max(1, len(nodes)))(*[_c_node(nd, keep) for nd in nodes])
+        inits = []
+        for name, arr in initializers.items():
+            a = np.ascontiguousarray(arr, dtype=np.float32)
+            keep.append(a)
+            t = C.TensorInfo()
+            t.name = name.encode()
+            keep.append(t.name)
+            t.data = a.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+            shp = C.i64_array(a.shape)
+            keep.append(shp)
+            t.shape = ctypes.cast(shp, ctypes.POINTER(ctypes.c_int64))
+            t.rank = a.ndim
+            inits.append(t)
+        init_arr = (C.TensorInfo * max(1, len(inits)))(*inits)
+        ins = []
+        for name, shape in self.input_specs:
+            t = C.TensorInfo()
+            t.name = name.encode()
+            keep.append(t.name)
+            shp = C.i64_array(shape)
+            keep.append(shp)
+            t.shape = ctypes.cast(shp, ctypes.POINTER(ctypes.c_int64))
+            t.rank = len(shape)
+            ins.append(t)
+        in_arr = (C.TensorInfo * max(1, len(ins)))(*ins)
+        onames = [o.encode() for o in outputs]
+        out_arr = (ctypes.c_char_p * max(1, len(onames)))(*onames)
+        ptr = ctypes.c_void_p()
+        handle.check(C.lib().onnxb200_graph_build(handle.ptr, cnodes, len(nodes), init_arr, len(inits), in_arr,
+                                                  len(ins), out_arr, len(onames), ctypes.byref(ptr)), "graph build")
+        self.ptr = ptr
+        self.output_shapes = []
+        for i in range(len(outputs)):
+            shp = C.i64_array([0] * 8)
+            r = ctypes.c_int()
+            handle.check(C.lib().onnxb200_graph_output_shape(self.ptr, i, shp, ctypes.byref(r)))
+            self.output_shapes.append([int(v) for v in shp[:r.value]])
+
+    def stats(self) -> dict:
+        s = C.GraphStats()
+        self.handle.check(C.lib().onnxb200_graph_get_stats(self.ptr, ctypes.byref(s)))
+        return {f: getattr(s, f) for f, _ in C.GraphStats._fields_}
+
+    def alloc_outputs(self, device) -> List[torch.Tensor]:
+        return [torch.empty(s, dtype=torch.float32, device=device) for s in self.output_shapes]
+
+    def run(self, inputs: Sequence[torch.Tensor], outputs: Sequence[torch.Tensor] | None = None) -> List[torch.Tensor]:
+        """Asynchronous run on device tensors (NCHW)."""
+        if outputs is None:
+            outputs = self.alloc_outputs(inputs[0].device)
+        for t, (name, shape) in zip(inputs, self.input_specs):
+            if list(t.shape) != shape:
+                raise ValueError(f"input {name}: expected shape {shape}, got {list(t.shape)}")
+        iarr = (ctypes.c_void_p * max(1, len(inputs)))(*[t.data_ptr() for t in inputs])
+        oarr = (ctypes.c_void_p * max(1, len(outputs)))(*[t.data_ptr() for t in outputs])
+        self.handle.check(C.lib().onnxb200_graph_run(self.handle.ptr, self.ptr, iarr, oarr), "graph run")
+        return list(outputs)
+
+    def run_host(self, inputs: Sequence[np.ndarray | torch.Tensor],
+                 outputs: Sequence[np.ndarray | torch.Tensor] | None = None):
+        """Host buffers in and out (copies inside); returns after the results are on the host."""
+        ins = [np.ascontiguousarray(x, dtype=np.float32) if isinstance(x, np.ndarray) else x for x in inputs]
+        if outputs is None:
+            outputs = [np.empty(s, np.float32) for s in self.output_shapes]
+
+        def addr(t):
+            return t.ctypes.data if isinstance(t, np.ndarray) else t.data_ptr()
+
+        iarr = (ctypes.c_void_p * max(1, len(ins)))(*[addr(t) for t in ins])
+        oarr = (ctypes.c_void_p * max(1, len(outputs)))(*[addr(t) for t in outputs])
+        self.handle.check(C.lib().onnxb200_graph_run_host(self.handle.ptr, self.ptr, iarr, oarr), "graph run_host")
+        return list(outputs)
+
+    def profile(self, inputs: Sequence[torch.Tensor], outputs: Sequence[torch.Tensor] | None = None) -> List[dict]:
+        """One eager run with CUDA events around every step; returns per-step
+        {kind, ms, flops, bytes} (algorithmic work)."""
+        if outputs is None:
+            outputs = self.alloc_outputs(inputs[0].device)
+        iarr = (ctypes.c_void_p * max(1, len(inputs)))(*[t.data_ptr() for t in inputs])
+        oarr = (ctypes.c_void_p * max(1, len(outputs)))(*[t.data_ptr() for t in outputs])
+        cap = 4096
+        prof = (C.StepProfile * cap)()
+        n = ctypes.c_int()
+        self.handle.check(C.lib().onnxb200_graph_profile(self.handle.ptr, self.ptr, iarr, oarr, prof, cap,
+                                                         ctypes.byref(n)), "graph profile")
+        return [{"kind": C.STEP_KINDS.get(p.kind, str(p.kind)), "ms": p.ms, "flops": p.flops, "bytes": p.bytes}
+                for p in prof[:min(n.value, cap)]]
+
+    def close(self):
+        if getattr(self, "ptr", None):
+            C.lib().onnxb200_graph_destroy(self.ptr)
+            self.ptr = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,134 @@
+"""CPU tests of the C ABI: the library loads, exports exactly what include/onnxb200.h
+declares, and its host-only entry points (shape inference, status strings) agree
+with the oracle.  No kernel is launched."""
+import ctypes
+import os
+import re
+import subprocess
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "onnxb200.h")
+
+
+def declared_symbols():
+    src = open(HEADER).read()
+    return sorted(set(re.findall(r"ONNXB200_API\s+[\w\s\*]+?\b(onnxb200_\w+)\s*\(", src)))
+
+
+def test_library_loads_and_exports_header(ob):
+    lib = ob._capi.lib()
+    decl = declared_symbols()
+    assert len(decl) >= 30
+    for name in decl:
+        assert hasattr(lib, name), name
+    out = subprocess.run(["nm", "-D", "--defined-only", ob.LIB_PATH], capture_output=True, text=True).stdout
+    exported = sorted(l.split()[-1] for l in out.splitlines() if " T " in l)
+    assert exported == decl
+    assert set(ob._capi.SIGNATURES) == set(decl)
+
+
+def test_version_and_status_strings(ob):
+    lib = ob._capi.lib()
+    assert lib.onnxb200_version() >= 100
+    assert lib.onnxb200_status_string(0) == b"ok"
+    assert lib.onnxb200_status_string(4) == b"operation timed out"
+    assert lib.onnxb200_last_error(None) == b"null handle"
+
+
+def test_null_arguments_rejected(ob):
+    lib = ob._capi.lib()
+    assert lib.onnxb200_create(0, None, None) == ob._capi.ERR_INVALID_ARGUMENT
+    assert lib.onnxb200_destroy(None) == ob._capi.ERR_INVALID_ARGUMENT
+    assert lib.onnxb200_synchronize(None) == ob._capi.ERR_INVALID_ARGUMENT
+    assert lib.onnxb200_graph_destroy(None) == ob._capi.ERR_INVALID_ARGUMENT
+
+
+@pytest.mark.parametrize("cfg", [
+    # x shape, w shape, strides, pads, dilations, group, auto_pad
+    ((1, 3, 224, 224), (64, 3, 7, 7), (2, 2), (3, 3, 3, 3), (1, 1), 1, "NOTSET"),
+    ((1, 1, 5, 5), (1, 1, 2, 2), (1, 1), (0, 0, 0, 0), (2, 2), 1, "NOTSET"),
+    ((1, 1, 5, 5), (1, 1, 2, 2), (2, 2), (0, 0, 0, 0), (1, 1), 1, "NOTSET"),
+    ((1, 1, 3, 3), (1, 1, 3, 3), (1, 1), (0, 0, 0, 0), (1, 1), 1, "SAME_UPPER"),
+    ((1, 1, 3, 3), (1, 1, 3, 3), (1, 1), (0, 0, 0, 0), (1, 1), 1, "VALID"),
+    ((2, 128, 28, 28), (128, 4, 3, 3), (1, 1), (1, 1, 1, 1), (1, 1), 32, "NOTSET"),
+    ((2, 256, 28, 28), (256, 256, 3, 3), (1, 1), (2, 2, 2, 2), (2, 2), 1, "NOTSET"),
+    ((3, 8, 224, 224), (16, 8, 7, 7), (2, 2), (0, 0, 0, 0), (1, 1), 1, "SAME_LOWER"),
+])
+def test_conv_output_shape_matches_oracle(ob, oracle, cfg):
+    xs, ws, st, pd, dl, g, ap = cfg
+    conv = ob.Conv(st, pd, dl, g, ap)
+    shape = conv.output_shape(xs, ws)
+    if ap in ("SAME_UPPER", "SAME_LOWER"):
+        up = ap == "SAME_UPPER"
+        pt, pb = oracle.same_pads(xs[2], ws[2], st[0], dl[0], up)
+        pl, pr = oracle.same_pads(xs[3], ws[3], st[1], dl[1], up)
+    elif ap == "VALID":
+        pt = pl = pb = pr = 0
+    else:
+        pt, pl, pb, pr = pd
+    exp = [xs[0], ws[0], oracle.conv_out_dim(xs[2], ws[2], st[0], pt, pb, dl[0]),
+           oracle.conv_out_dim(xs[3], ws[3], st[1], pl, pr, dl[1])]
+    assert shape == exp
+
+
+def test_conv_output_shape_rejects_bad_groups(ob):
+    with pytest.raises(ob.ValidationError):
+        ob.Conv(group=3).output_shape((1, 8, 5, 5), (4, 2, 3, 3))
+
+
+def test_matmul_output_shape_matches_oracle(ob, oracle):
+    cases = [((2, 3), (3, 4)), ((3,), (3,)), ((3,), (3, 2)), ((2, 3), (3,)), ((2, 3, 4), (2, 4, 5)),
+             ((2, 1, 3, 4), (2, 5, 4, 5)), ((3, 4), (2, 4, 5)), ((8, 1, 512, 768), (12, 768, 3072))]
+    for a, b in cases:
+        assert ob.MatMul.output_shape(a, b) == oracle.matmul_shape(a, b)
+    for a, b in [((2, 3), (4, 5)), ((2,), (3,)), ((2, 3, 4), (3, 4, 5)), ((5, 10, 20), (10, 20, 30))]:
+        with pytest.raises(ob.ValidationError):
+            ob.MatMul.output_shape(a, b)
+
+
+def test_registry_resolves_versions(ob):
+    r = ob.OperatorRegistry.initialize_standard_operators()
+    op = r.create_operator_for_node({"op": "Conv", "inputs": ["x", "w"], "outputs": ["y"],
+                                     "attrs": {"strides": [2, 2], "pads": [3, 3, 3, 3]}}, opset=13)
+    assert isinstance(op, ob.Conv) and op.strides == [2, 2] and op.pads == [3, 3, 3, 3]
+    with pytest.raises(ob.InvalidOperator):
+        r.create_operator_for_node({"op": "Conv", "inputs": [], "outputs": []}, opset=10)
+    with pytest.raises(ob.InvalidOperator):
+        r.create_operator_for_node({"op": "Softmax", "inputs": [], "outputs": []})
+    with pytest.raises(ob.InvalidOperator):
+        r.register_operator("Conv", "", 11, ob.Conv)
+    mp = r.create_operator_for_node({"op": "MaxPool", "attrs": {"kernel_shape": [3, 3], "strides": [2, 2],
+                                                                "pads": [1, 1, 1, 1]}})
+    assert mp.output_shapes({"attrs": {"kernel_shape": [3, 3], "strides": [2, 2], "pads": [1, 1, 1, 1]}},
+                            [[2, 64, 112, 112]]) == [[2, 64, 56, 56]]
+
+
+def test_synth_is_deterministic(ob):
+    a = ob.synth.normal(4, "X", (3, 5))
+    b = ob.synth.normal(4, "X", (3, 5))
+    c = ob.synth.normal(4, "Y", (3, 5))
+    np.testing.assert_array_equal(a, b)
+    assert not np.array_equal(a, c)
+    u = ob.synth.uniform(0, "X", (10000,), -1, 1)
+    assert u.min() >= -1 and u.max() < 1 and abs(u.mean()) < 0.05
+    n = ob.synth.normal(1, "A", (100000,))
+    assert abs(n.mean()) < 0.02 and abs(n.std() - 1) < 0.02
+
+
+def test_workload_graphs_are_well_formed(ob):
+    for build in (ob.workloads.resnet18, ob.workloads.resnet50):
+        nodes, inits, ins, outs = build(batch=2)
+        produced = {n["outputs"][0] for n in nodes}
+        for n in nodes:
+            for i in n["inputs"]:
+                assert i in produced or i in inits or i == ins[0][0], i
+        assert outs[0] in produced
+    nodes, _, _, _ = ob.workloads.resnet50(batch=1)
+    assert sum(1 for n in nodes if n["op"] == "Conv") == 53
+    # 4.09 GMAC per image for ResNet-50 v1.5 convolutions
+    assert abs(ob.workloads.resnet50.conv_flops_per_image / 2 - 4.09e9) / 4.09e9 < 0.02
+    nodes, _, _, _ = ob.workloads.resnet18(batch=1)
+    assert sum(1 for n in nodes if n["op"] == "Conv") == 20
