@@ -147,10 +147,113 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def time_on_stream(fn, steps, warmup, stream, flush=None):
+    """Mean device ms of fn() over `steps` runs: CUDA events on `stream` around
+    each call, an L2-evicting memset before each (outside the events)."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    evs = []
+    for _ in range(steps):
+        if flush is not None:
+            flush.zero_()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        evs.append((e0, e1))
+    torch.cuda.synchronize()
+    return sum(a.elapsed_time(b) for a, b in evs) / len(evs)
+
+
+def run_single_workload(args):
+    """One of the path's other workloads on one GPU (conv shapes, stem, MatMul, ResNet-18)."""
+    import importlib
+    import numpy as np
+    import torch
+    ob = importlib.import_module("onnx-rs_b200")
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    h = ob.Handle(0, precision=args.precision)
+    ctx = ob.ExecutionContext(h)
+    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device="cuda")
+    peaks, peak_src = load_peaks()
+    bf16 = peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
+    tpeak = {"3xtf32": bf16 / 6.0, "tf32": bf16 / 2.0, "bf16": bf16, "fp32": bf16 / 2.0}[args.precision]
+    wl = args.workload
+    if wl.startswith("conv:") or wl == "stem":
+        if wl == "stem":
+            nodes, inits, ins, outs = ob.workloads.stem_conv(0, batch=args.batch if args.batch != GLOBAL_BATCH else 1)
+            x = ob.workloads.stem_input(0, ins[0][1][0])
+            w, b = inits["W"], inits["B"]
+            attrs = {"strides": (2, 2), "pads": (3, 3, 3, 3), "dilations": (1, 1), "group": 1}
+        else:
+            x, w, b, attrs = ob.workloads.sweep_case(wl[5:], batch=128 if args.batch == GLOBAL_BATCH else args.batch)
+        conv = ob.Conv(attrs["strides"], attrs["pads"], attrs["dilations"], attrs["group"], relu=True)
+        n, c, hh, ww = x.shape
+        cs = c if c % 4 == 0 else (c + 3) // 4 * 4
+        xn = np.zeros((n, hh, ww, cs), np.float32)
+        xn[..., :c] = x.transpose(0, 2, 3, 1)
+        wt = torch.from_numpy(w).cuda()
+        bt = torch.from_numpy(b).cuda()
+        xt = torch.from_numpy(xn).cuda()
+        if cs != c:  # channel-padded NHWC input: pad the weights with zero input channels too
+            wp = np.zeros((w.shape[0], cs, w.shape[2], w.shape[3]), np.float32)
+            wp[:, :c] = w
+            wt = torch.from_numpy(wp).cuda()
+        plan = ob.ConvPlan(ctx, conv, (n, hh, ww, cs), wt, bt, layout=1)
+        y = torch.empty(plan.out_shape, dtype=torch.float32, device="cuda")
+        ms = time_on_stream(lambda: plan.run(xt, y), args.steps, args.warmup, stream, flush)
+        _, oh, ow, co = plan.out_shape
+        flops = 2.0 * n * oh * ow * co * (c // attrs["group"]) * w.shape[2] * w.shape[3]
+        bytes_ = 4.0 * (n * hh * ww * c + w.size + co + n * oh * ow * co)
+        name = "stem_conv7x7s2_relu" if wl == "stem" else wl[5:]
+        metric, value, unit = "conv TFLOP/s", flops / ms / 1e9, "TFLOP/s"
+        plan.close()
+    elif wl in ("matmul", "resnet18"):
+        if wl == "matmul":
+            nodes, inits, ins, outs = ob.workloads.broadcast_matmul_graph(1)
+            a, _, _ = ob.workloads.broadcast_matmul(1)
+            x = torch.from_numpy(a).cuda()
+            flops = 2.0 * 96 * 512 * 3072 * 768
+            bytes_ = 4.0 * (a.size + 12 * 768 * 3072 + 3072 + 96 * 512 * 3072)
+            name, metric, unit = "broadcast_matmul_add_relu", "MatMul TFLOP/s", "TFLOP/s"
+        else:
+            bsz = 32 if args.batch == GLOBAL_BATCH else args.batch
+            nodes, inits, ins, outs = ob.workloads.resnet18(batch=bsz, seed=2)
+            x = torch.from_numpy(ob.workloads.resnet_input(2, bsz)).cuda()
+            flops = ob.workloads.resnet18.conv_flops_per_image * bsz
+            bytes_ = None
+            name, metric, unit = f"resnet18_b{bsz}", "ResNet-18 images/s", "images/s"
+        g = ob.Graph(h, nodes, inits, ins, outs)
+        yout = g.alloc_outputs(x.device)
+        ms = time_on_stream(lambda: g.run([x], yout), args.steps, args.warmup, stream, flush)
+        value = flops / ms / 1e9 if unit == "TFLOP/s" else ins[0][1][0] / (ms / 1e3)
+        g.close()
+    else:
+        raise SystemExit(f"unknown workload {wl}")
+    tf = flops / ms / 1e9
+    line = {"metric": metric, "value": value, "unit": unit, "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "precision": args.precision,
+            "data": "synthetic", "config": {"workload": name, "l2": "flushed between timed steps"},
+            "roofline": {"tensor": {"achieved": tf, "peak": tpeak, "unit": "TFLOP/s", "frac": tf / tpeak},
+                         "hbm": None if bytes_ is None else
+                         {"achieved": bytes_ / ms / 1e6, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                          "frac": bytes_ / ms / 1e6 / peaks["hbm_gbs"]},
+                         "peak_source": peak_src},
+            "gpu_launches": None}
+    print(json.dumps(line), flush=True)
+    h.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--workload", default="resnet50",
+                    help="resnet50 (headline) | resnet18 | stem | matmul | conv:<sweep shape name>")
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--precision", default="3xtf32", choices=["3xtf32", "tf32", "bf16", "fp32"])
@@ -162,6 +265,9 @@ def main():
         run_reference(args)
         return
     args.warmup = max(args.warmup, 3)
+    if args.workload != "resnet50":
+        run_single_workload(args)
+        return
 
     import importlib
     import numpy as np
@@ -195,11 +301,15 @@ def main():
     xs = np.ascontiguousarray(xfull[rank * per_rank:(rank + 1) * per_rank])
     del xfull
 
+    # one dedicated stream: the library's kernels, the L2 flush and the CUDA
+    # events all go on it
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
     h = ob.Handle(local, precision=args.precision)
+    assert h.stream_ptr == stream.cuda_stream
     g = ob.Graph(h, nodes, inits, ins, outs)
     xin = torch.from_numpy(xs).cuda()
     yout = g.alloc_outputs(xin.device)
-    stream = torch.cuda.current_stream()
 
     for _ in range(args.warmup):
         g.run([xin], yout)
@@ -211,6 +321,7 @@ def main():
     flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device="cuda")
     clocks = ClockSampler(local)
     clocks.start()
+    time.sleep(0.5)  # let nvidia-smi start sampling before the timed region
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     barrier()

@@ -96,7 +96,8 @@ ONNXB200_API int onnxb200_destroy(onnxb200_handle* h);
 ONNXB200_API const char* onnxb200_last_error(const onnxb200_handle* h);
 /* Message for a status code. */
 ONNXB200_API const char* onnxb200_status_string(int status);
-/* Runs subsequent work on a caller-owned cudaStream_t (NULL = handle's own stream). */
+/* Runs subsequent work on a caller-owned cudaStream_t (NULL = the handle's own
+ * stream, a blocking stream ordered with the legacy default stream). */
 ONNXB200_API int onnxb200_set_stream(onnxb200_handle* h, void* cuda_stream);
 ONNXB200_API void* onnxb200_get_stream(onnxb200_handle* h);
 /* Waits for the handle's stream (bounded) and checks the device status word. */

@@ -9,7 +9,7 @@ reference's operator interface over that ABI.  Import it with
 from . import _capi
 from .runtime import (Handle, OnnxB200Error, ValidationError, ExecutionError, UnsupportedFeature,
                       OperationTimeout, ResourceExhausted, InvalidGraph, InvalidOperator)
-from .ops import (ExecutionContext, Operator, OperatorRegistry, Conv, MatMul, Gemm, MaxPool,
+from .ops import (ExecutionContext, Operator, OperatorRegistry, Conv, ConvPlan, MatMul, Gemm, MaxPool,
                   GlobalAveragePool, Relu, Add, BatchNormalization, Flatten)
 from .graph import Graph
 from . import synth, workloads
@@ -18,5 +18,5 @@ LIB_PATH = _capi.LIB_PATH
 
 __all__ = ["Handle", "OnnxB200Error", "ValidationError", "ExecutionError", "UnsupportedFeature",
            "OperationTimeout", "ResourceExhausted", "InvalidGraph", "InvalidOperator", "ExecutionContext",
-           "Operator", "OperatorRegistry", "Conv", "MatMul", "Gemm", "MaxPool", "GlobalAveragePool", "Relu",
+           "Operator", "OperatorRegistry", "Conv", "ConvPlan", "MatMul", "Gemm", "MaxPool", "GlobalAveragePool", "Relu",
            "Add", "BatchNormalization", "Flatten", "Graph", "synth", "workloads", "LIB_PATH"]

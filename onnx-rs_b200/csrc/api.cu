@@ -6,6 +6,7 @@
 #include <algorithm>
 #include <chrono>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <new>
 #include <string>
@@ -410,6 +411,8 @@ int onnxb200_create(int device, const onnxb200_options* opts, onnxb200_handle** 
     if (h->opts.precision < 0 || h->opts.precision > 3) h->opts.precision = ONNXB200_PREC_3XTF32;
   }
   h->device = device;
+  const char* dbg = std::getenv("ONNXB200_DEBUG_SYNC");
+  h->debug_sync = dbg && dbg[0] == '1';
   int rc = ONNXB200_OK;
   cudaError_t e = cudaSetDevice(device);
   if (e == cudaSuccess) {
@@ -421,7 +424,10 @@ int onnxb200_create(int device, const onnxb200_options* opts, onnxb200_handle** 
       return ONNXB200_ERR_UNSUPPORTED;  // built for sm_100a only
     }
     cudaDeviceGetAttribute(&h->num_sms, cudaDevAttrMultiProcessorCount, device);
-    e = cudaStreamCreateWithFlags(&h->own_stream, cudaStreamNonBlocking);
+    // A blocking stream: work on it is ordered with the legacy default stream,
+    // so callers that use the default stream (torch's default, plain
+    // cudaMemcpy) see results in order without extra synchronisation.
+    e = cudaStreamCreateWithFlags(&h->own_stream, cudaStreamDefault);
   }
   if (e == cudaSuccess) {
     h->stream = h->own_stream;
@@ -583,7 +589,7 @@ int onnxb200_conv_plan_run(onnxb200_handle* h, const onnxb200_conv_plan* p, cons
 int onnxb200_conv2d(onnxb200_handle* h, const onnxb200_conv_desc* d, const float* x,
                     const float* w, const float* bias, const float* bn_scale, const float* bn_bias,
                     const float* bn_mean, const float* bn_var, const float* residual, float* y) {
-  if (!h || !d || !x || !w || !y) return set_error(h, ONNXB200_ERR_INVALID_ARGUMENT, "Conv: null argument");
+  if (!h || !d) return set_error(h, ONNXB200_ERR_INVALID_ARGUMENT, "Conv: null argument");
   cudaSetDevice(h->device);
   const int cs = d->layout == ONNXB200_LAYOUT_NHWC ? (int)d->c : (int)((d->c + 3) / 4 * 4);
   // Packed weights go to the front of the workspace; activation repacks follow.
@@ -591,6 +597,8 @@ int onnxb200_conv2d(onnxb200_handle* h, const onnxb200_conv_desc* d, const float
   int64_t oh, ow;
   int rc = resolve_conv_desc(h, d, &r, &oh, &ow);
   if (rc) return rc;
+  if (r.n == 0) return ONNXB200_OK;  // empty batch: nothing to compute (buffers may be null)
+  if (!x || !w || !y) return set_error(h, ONNXB200_ERR_INVALID_ARGUMENT, "Conv: null argument");
   const size_t wneed = align_up((size_t)r.c_out * ((r.kh * r.kw * cs + 31) / 32 * 32) * 4) * 2 +
                        align_up((size_t)r.c_out * (r.c / r.group) * r.kh * r.kw * 4) +
                        2 * align_up(r.c_out * 4) + kAlign;

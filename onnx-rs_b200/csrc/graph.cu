@@ -56,13 +56,14 @@ struct GTensor {
   int producer = -1;           // step index
   int last_use = -1;           // step index
   int alias_of = -1;           // Flatten view of another tensor
+  bool nhwc = false;           // rank-4 image tensor stored NHWC (else row-major as given)
   int64_t numel() const {
     int64_t n = 1;
     for (auto v : shape) n *= v;
     return n;
   }
   size_t bytes() const {
-    if (shape.size() == 4) return (size_t)shape[0] * shape[2] * shape[3] * (cs ? cs : shape[1]) * 4;
+    if (nhwc) return (size_t)shape[0] * shape[2] * shape[3] * (cs ? cs : shape[1]) * 4;
     return (size_t)numel() * 4;
   }
 };
@@ -123,6 +124,7 @@ struct GemmPlan {
 
 struct onnxb200_graph {
   onnxb200_handle* h = nullptr;
+  int device = 0;
   std::vector<GTensor> tensors;
   std::vector<Step> steps;
   std::vector<onnxb200_conv_plan> plans;
@@ -151,7 +153,8 @@ namespace {
 
 int fail(onnxb200_handle* h, int code, const std::string& msg) { return set_error(h, code, msg); }
 
-bool is_rank4(const GTensor& t) { return t.shape.size() == 4; }
+// Image tensors (rank 4, produced or consumed by image ops) live in NHWC.
+bool is_rank4(const GTensor& t) { return t.nhwc; }
 
 // Storage strides of a tensor in the iteration order used by add kernels:
 // rank-4 tensors are iterated as (N, H, W, C) over their NHWC storage.
@@ -188,10 +191,10 @@ static void destroy_graph(onnxb200_graph* g) {
 
 extern "C" int onnxb200_graph_destroy(onnxb200_graph* g) {
   if (!g) return ONNXB200_ERR_INVALID_ARGUMENT;
-  if (g->h) {
-    cudaSetDevice(g->h->device);
-    cudaStreamSynchronize(g->h->stream);
-  }
+  // The graph may outlive its handle (and the handle's stream): wait on the
+  // whole device instead of touching the handle.
+  cudaSetDevice(g->device);
+  cudaDeviceSynchronize();
   destroy_graph(g);
   return ONNXB200_OK;
 }
@@ -206,6 +209,7 @@ extern "C" int onnxb200_graph_build(onnxb200_handle* h, const onnxb200_node* nod
   onnxb200_graph* g = new (std::nothrow) onnxb200_graph();
   if (!g) return ONNXB200_ERR_RESOURCE_EXHAUSTED;
   g->h = h;
+  g->device = h->device;
   g->n_nodes_in = n_nodes;
   std::map<std::string, int> by_name;
   auto tensor_id = [&](const std::string& name) -> int {
@@ -411,14 +415,16 @@ extern "C" int onnxb200_graph_build(onnxb200_handle* h, const onnxb200_node* nod
         consumer_nodes[t].push_back(i);
       }
   for (int t : g->outputs) consumers[t]++;
+  std::vector<int> absorbed(n_nodes, 0);
+  // The single consumer of `t` if it is an `op` node not yet absorbed into
+  // another fused step (a residual Add has two producers that could claim it;
+  // the first in topological order wins).
   auto sole_consumer = [&](int t, const char* op) -> int {
     if (consumers[t] != 1 || consumer_nodes[t].size() != 1) return -1;
     const int c = consumer_nodes[t][0];
-    return nodes[c].op == op ? c : -1;
+    return (nodes[c].op == op && !absorbed[c]) ? c : -1;
   };
   auto is_const = [&](int t) { return t >= 0 && g->tensors[t].is_init; };
-  std::vector<int> pos(n_nodes);
-  for (int i = 0; i < n_nodes; ++i) pos[order[i]] = i;
 
   struct Fused {
     int head;                 // node index of the contraction (or op)
@@ -428,7 +434,6 @@ extern "C" int onnxb200_graph_build(onnxb200_handle* h, const onnxb200_node* nod
     int bias_add = -1;        // MatMul bias Add node
     int out = -1;
   };
-  std::vector<int> absorbed(n_nodes, 0);
   std::vector<Fused> fused_at(n_nodes, Fused{-1, -1});
   for (int idx : order) {
     if (absorbed[idx]) continue;
@@ -495,13 +500,55 @@ extern "C" int onnxb200_graph_build(onnxb200_handle* h, const onnxb200_node* nod
         absorbed[c] = 1;
       }
     }
+    if (fused_at[f.last].head >= 0)
+      return bail(ONNXB200_ERR_INVALID_GRAPH, "internal: two fused steps end at node " + nodes[f.last].op);
     fused_at[f.last] = f;
   }
   for (int i = 0; i < n_nodes; ++i) g->n_fused += absorbed[i];
 
   // ---------------------------------------------------------------- layout (channel strides)
-  for (auto& t : g->tensors)
-    if (is_rank4(t) && !t.is_init) t.cs = (int)t.shape[1];
+  // Rank-4 activations are images in NHWC unless a MatMul / Gemm reads or
+  // writes them (those keep their row-major numpy layout).
+  {
+    std::vector<char> plain(g->tensors.size(), 0);
+    for (int i = 0; i < n_nodes; ++i)
+      if (nodes[i].op == "MatMul" || nodes[i].op == "Gemm") {
+        for (int t : nodes[i].in)
+          if (t >= 0) plain[t] = 1;
+        for (int t : nodes[i].out) plain[t] = 1;
+      }
+    // elementwise ops keep the layout of their operands
+    for (int i : order) {
+      const Node& nd = nodes[i];
+      if (nd.op != "Add" && nd.op != "Relu") continue;
+      bool any_plain = false;
+      for (int t : nd.in)
+        if (t >= 0 && !g->tensors[t].is_init && plain[t]) any_plain = true;
+      if (any_plain)
+        for (int t : nd.out) plain[t] = 1;
+    }
+    for (int i : order) {
+      const Node& nd = nodes[i];
+      if (nd.op != "Add" && nd.op != "Relu") continue;
+      for (int t : nd.in)
+        if (t >= 0 && !g->tensors[t].is_init && g->tensors[t].shape.size() == 4 && plain[t] != plain[nd.out[0]])
+          return bail(ONNXB200_ERR_UNSUPPORTED, "elementwise op mixing image and MatMul layouts: " + nd.op);
+    }
+    for (int i = 0; i < n_nodes; ++i) {
+      const bool image_op = nodes[i].op == "Conv" || nodes[i].op == "MaxPool" ||
+                            nodes[i].op == "GlobalAveragePool" || nodes[i].op == "BatchNormalization";
+      if (!image_op) continue;
+      for (int t : nodes[i].in)
+        if (t >= 0 && plain[t] && !g->tensors[t].is_init)
+          return bail(ONNXB200_ERR_UNSUPPORTED, "tensor used both as an image and as a MatMul operand: " +
+                                                    g->tensors[t].name);
+    }
+    for (size_t t = 0; t < g->tensors.size(); ++t) {
+      GTensor& tt = g->tensors[t];
+      tt.nhwc = tt.shape.size() == 4 && !tt.is_init && !plain[t];
+      if (tt.nhwc) tt.cs = (int)tt.shape[1];
+    }
+  }
   for (int id : g->inputs) {
     GTensor& t = g->tensors[id];
     if (!is_rank4(t) || t.shape[1] % 4 == 0) continue;
@@ -687,9 +734,9 @@ extern "C" int onnxb200_graph_build(onnxb200_handle* h, const onnxb200_node* nod
       const int r = (int)od.size();
       auto align_op = [&](const GTensor& t, long long* strides) {
         std::vector<int64_t> d, st;
-        if (is_rank4(t) && r == 4) {
+        if (t.nhwc && O.nhwc) {
           storage_view(t, d, st);
-        } else if (r == 4) {
+        } else if (O.nhwc) {
           // a lower-rank constant broadcast against NHWC storage: map its NCHW
           // dims (right-aligned) onto (N, H, W, C)
           std::vector<int64_t> nchw(4, 1);
@@ -782,6 +829,17 @@ extern "C" int onnxb200_graph_build(onnxb200_handle* h, const onnxb200_node* nod
   for (auto& t : g->tensors)
     if (t.alias_of >= 0) t.off = g->tensors[base_of(t.alias_of)].off;
   g->arena_bytes = arena;
+  // every activation a step touches must have been produced and placed
+  for (const Step& s : g->steps) {
+    std::vector<int> ids = s.in;
+    if (s.out >= 0) ids.push_back(s.out);
+    for (int t : ids) {
+      if (t < 0) continue;
+      const GTensor& tt = g->tensors[t];
+      if (!tt.is_init && tt.off < 0)
+        return bail(ONNXB200_ERR_INVALID_GRAPH, "internal: tensor without storage: " + tt.name);
+    }
+  }
 
   // ---------------------------------------------------------------- device memory
   g->init_bytes = init_total + extra;
@@ -805,8 +863,13 @@ extern "C" int onnxb200_graph_build(onnxb200_handle* h, const onnxb200_node* nod
     const PendingConv& pc = pconv[i];
     const GTensor& xt = g->tensors[pc.x];
     size_t need = 0;
-    int rc = conv_plan_init(h, &pc.d, xt.cs ? xt.cs : (int)xt.shape[1], dptr(pc.w), nullptr, nullptr, nullptr,
-                            nullptr, nullptr, &g->plans[pc.plan], nullptr, 0, &need);
+    const float *qb = pc.b >= 0 ? dptr(pc.b) : nullptr, *q1 = nullptr, *q2 = nullptr, *q3 = nullptr, *q4 = nullptr;
+    if (pc.bn >= 0) {
+      const Node& bn = nodes[pc.bn];
+      q1 = dptr(bn.in[1]); q2 = dptr(bn.in[2]); q3 = dptr(bn.in[3]); q4 = dptr(bn.in[4]);
+    }
+    int rc = conv_plan_init(h, &pc.d, xt.cs ? xt.cs : (int)xt.shape[1], dptr(pc.w), qb, q1, q2, q3, q4,
+                            &g->plans[pc.plan], nullptr, 0, &need);
     if (rc) { destroy_graph(g); return rc; }
     plan_off[i] = wtotal;
     wtotal += align_up(need);
@@ -1054,6 +1117,20 @@ static int run_steps(onnxb200_graph* g, const float* const* uin, float* const* u
     }
     if (rc) return cuda_check(h, (cudaError_t)rc, "graph step");
     if (ev) cudaEventRecord((*ev)[2 * si + 1], st);
+    if (h->debug_sync) {
+      cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+      cudaStreamIsCapturing(st, &cs);
+      if (cs == cudaStreamCaptureStatusNone) {
+        cudaError_t e = cudaStreamSynchronize(st);
+        if (e != cudaSuccess) {
+          const int out_id = s.out >= 0 ? s.out : (s.in.empty() ? -1 : s.in[0]);
+          return set_error(h, ONNXB200_ERR_EXECUTION,
+                           "step " + std::to_string(si) + " (type " + std::to_string((int)s.type) +
+                               ", tensor " + (out_id >= 0 ? g->tensors[out_id].name : std::string("?")) +
+                               "): " + cudaGetErrorString(e));
+        }
+      }
+    }
   }
   return ONNXB200_OK;
 }

@@ -70,7 +70,18 @@ struct Layout {
   static constexpr int kNumBars = 2 * kStages + 5;
   static constexpr int kMisc = kBar + kNumBars * 8;   // tmem base (4B) + abort flag (4B)
   static constexpr int kBytes = kMisc + 16 + 1024;    // + alignment slack
-  static constexpr int kTmemCols = (2 * BN < 32) ? 32 : 2 * BN;
+  // 3xTF32 "promotion": the tensor core adds into its fp32 accumulator with
+  // truncation, so a long K-loop into one accumulator drifts by ~1 ulp per MMA.
+  // In 3xTF32 mode each accumulator therefore only sums kChunkKB k-blocks
+  // (24 MMAs); the epilogue warps fold the chunks into a running total with
+  // round-to-nearest adds.  TMEM: total [0, BN), chunks [BN, 2BN) and [2BN, 3BN).
+  // Other modes: two whole-tile accumulators [0, BN) and [BN, 2BN).
+  static constexpr bool kPromote = (PREC == kPrec3xTF32);
+  static constexpr int kChunkKB = kPromote ? 2 : (1 << 30);
+  static constexpr int kCols = kPromote ? 3 * BN : 2 * BN;
+  static constexpr int kTmemCols = kCols <= 32 ? 32 : kCols <= 64 ? 64 : kCols <= 128 ? 128
+                                   : kCols <= 256 ? 256 : 512;
+  static_assert(kCols <= 512, "accumulators exceed TMEM");
 };
 
 __device__ __forceinline__ uint32_t swz_off(int row, int chunk, int row_bytes) {
@@ -96,6 +107,38 @@ __device__ __forceinline__ float4 ldg_f4(const float* p) {
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Epilogue of 32 consecutive columns of one output row: y = acc * scale + shift
+// (+ residual) (relu), float4 stores.
+__device__ __forceinline__ void store_row32(const IgemmParams& p, const uint32_t (&r)[32], int col0,
+                                            float* yrow, const float* rrow) {
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const int c = col0 + 4 * q;
+    if (c < p.Nc) {
+      float v[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) v[e] = __uint_as_float(r[4 * q + e]);
+      if (p.scale) {
+        const float4 sc = *reinterpret_cast<const float4*>(p.scale + c);
+        v[0] *= sc.x; v[1] *= sc.y; v[2] *= sc.z; v[3] *= sc.w;
+      }
+      if (p.shift) {
+        const float4 sh = *reinterpret_cast<const float4*>(p.shift + c);
+        v[0] += sh.x; v[1] += sh.y; v[2] += sh.z; v[3] += sh.w;
+      }
+      if (rrow) {
+        const float4 rv = *reinterpret_cast<const float4*>(rrow + c);
+        v[0] += rv.x; v[1] += rv.y; v[2] += rv.z; v[3] += rv.w;
+      }
+      if (p.relu) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) v[e] = v[e] > 0.f ? v[e] : 0.f;
+      }
+      *reinterpret_cast<float4*>(yrow + c) = make_float4(v[0], v[1], v[2], v[3]);
+    }
+  }
 }
 
 template <int PREC, int BN>
@@ -290,16 +333,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr uint32_t idesc = make_idesc(PREC == kPrecBF16 ? 1 : 2, kBM, BN);
     int item = 0;
     bool issued = false;
+    uint32_t cc = 0;  // accumulator-chunk counter (3xTF32 promotion)
     for (int tj = 0; tj < my_tiles; ++tj) {
       const int buf = tj & 1;
       const uint32_t aph = (tj >> 1) & 1;
-      if (!mbar_wait(tempty_bar(buf), aph ^ 1, abort_flag, p.status)) break;
-      tc_fence_after();
-      const uint32_t d_tmem = tmem_base + buf * BN;
+      uint32_t d_tmem = tmem_base + buf * BN;
+      int cb = 0;
+      if constexpr (!L::kPromote) {
+        if (!mbar_wait(tempty_bar(buf), aph ^ 1, abort_flag, p.status)) break;
+        tc_fence_after();
+      }
       bool failed = false;
       for (int kb = 0; kb < p.num_kb; ++kb, ++item) {
         const int s = item % S;
         const uint32_t ph = (item / S) & 1;
+        const int kin = kb % L::kChunkKB;  // k-block index inside the accumulator chunk
+        if constexpr (L::kPromote) {
+          if (kin == 0) {
+            cb = cc & 1;
+            if (!mbar_wait(tempty_bar(cb), ((cc >> 1) & 1) ^ 1, abort_flag, p.status)) {
+              failed = true;
+              break;
+            }
+            tc_fence_after();
+            d_tmem = tmem_base + BN * (1 + cb);
+          }
+        }
         if (!mbar_wait(full_bar(s), ph, abort_flag, p.status)) {
           failed = true;
           break;
@@ -326,7 +385,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < C::kKSteps; ++kk) {
             const uint64_t step = (uint64_t)(kk * C::kDescStep);
-            const uint32_t acc = (kb | kk) ? 1u : 0u;
+            const uint32_t acc = ((L::kPromote ? kin : kb) | kk) ? 1u : 0u;
             tc_mma<PREC == kPrecBF16 ? 1 : 0>(d_tmem, fix(dah + step), fix(dbh + step), idesc, acc);
             if constexpr (C::kSplit) {
               tc_mma<0>(d_tmem, dah + step, dbl + step, idesc, 1u);
@@ -336,10 +395,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_commit(empty_bar(s));
           issued = true;
         }
+        if constexpr (L::kPromote) {
+          if (kin == L::kChunkKB - 1 || kb == p.num_kb - 1) {
+            if (lane == 0) tc_commit(tfull_bar(cb));
+            ++cc;
+          }
+        }
         __syncwarp();
       }
       if (failed) break;
-      if (lane == 0) tc_commit(tfull_bar(buf));
+      if constexpr (!L::kPromote) {
+        if (lane == 0) tc_commit(tfull_bar(buf));
+      }
       __syncwarp();
     }
     // Drain: every MMA issued by this thread has completed before TMEM is freed.
@@ -352,11 +419,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int row_in_tile = warp * 32 + lane;
+    const uint32_t lane_addr = (uint32_t)(warp * 32) << 16;
+    uint32_t cc = 0;
     for (int tj = 0; tj < my_tiles; ++tj) {
-      const int buf = tj & 1;
-      const uint32_t aph = (tj >> 1) & 1;
-      if (!mbar_wait(tfull_bar(buf), aph, abort_flag, p.status)) break;
-      tc_fence_after();
       int b, mt, nt;
       tile_coords(blockIdx.x + tj * gridDim.x, b, mt, nt);
       const int m = mt * kBM + row_in_tile;
@@ -364,44 +429,63 @@ __global__ void __launch_bounds__(kThreads, 1)
       float* yrow = p.y + (long long)b * p.y_bstride + (long long)m * p.ldy;
       const float* rrow =
           p.res ? p.res + (long long)b * p.y_bstride + (long long)m * p.ldr : nullptr;
-#pragma unroll 1
-      for (int j = 0; j < BN / 32; ++j) {
-        const int col0 = nt * BN + j * 32;
-        if (col0 >= p.Nc) break;  // warp-uniform
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(warp * 32) << 16) + buf * BN + j * 32, r);
-        tmem_ld_wait();
-        if (row_ok) {
-#pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const int c = col0 + 4 * q;
-            if (c < p.Nc) {
-              float v[4];
-#pragma unroll
-              for (int e = 0; e < 4; ++e) v[e] = __uint_as_float(r[4 * q + e]);
-              if (p.scale) {
-                const float4 sc = *reinterpret_cast<const float4*>(p.scale + c);
-                v[0] *= sc.x; v[1] *= sc.y; v[2] *= sc.z; v[3] *= sc.w;
-              }
-              if (p.shift) {
-                const float4 sh = *reinterpret_cast<const float4*>(p.shift + c);
-                v[0] += sh.x; v[1] += sh.y; v[2] += sh.z; v[3] += sh.w;
-              }
-              if (rrow) {
-                const float4 rv = *reinterpret_cast<const float4*>(rrow + c);
-                v[0] += rv.x; v[1] += rv.y; v[2] += rv.z; v[3] += rv.w;
-              }
-              if (p.relu) {
-#pragma unroll
-                for (int e = 0; e < 4; ++e) v[e] = v[e] > 0.f ? v[e] : 0.f;
-              }
-              *reinterpret_cast<float4*>(yrow + c) = make_float4(v[0], v[1], v[2], v[3]);
-            }
+      if constexpr (L::kPromote) {
+        // Fold each chunk accumulator into the running total (TMEM columns
+        // [0, BN)) with round-to-nearest fp32 adds; the last chunk goes straight
+        // to the output epilogue.
+        const int nch = (p.num_kb + L::kChunkKB - 1) / L::kChunkKB;
+        bool failed = false;
+        for (int ch = 0; ch < nch; ++ch, ++cc) {
+          const int cb = cc & 1;
+          if (!mbar_wait(tfull_bar(cb), (cc >> 1) & 1, abort_flag, p.status)) {
+            failed = true;
+            break;
           }
+          tc_fence_after();
+          const bool last = ch == nch - 1;
+#pragma unroll 1
+          for (int j = 0; j < BN / 32; ++j) {
+            const int col0 = nt * BN + j * 32;
+            if (col0 >= p.Nc) break;  // warp-uniform
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(tmem_base + lane_addr + BN * (1 + cb) + j * 32, r);
+            if (ch > 0) {
+              uint32_t t[32];
+              tmem_ld_32x32b_x32(tmem_base + lane_addr + j * 32, t);
+              tmem_ld_wait();
+#pragma unroll
+              for (int e = 0; e < 32; ++e)
+                r[e] = __float_as_uint(__uint_as_float(t[e]) + __uint_as_float(r[e]));
+            } else {
+              tmem_ld_wait();
+            }
+            if (!last)
+              tmem_st_32x32b_x32(tmem_base + lane_addr + j * 32, r);
+            else if (row_ok)
+              store_row32(p, r, col0, yrow, rrow);
+          }
+          if (!last) tmem_st_wait();
+          tc_fence_before();
+          mbar_arrive(tempty_bar(cb));
         }
+        if (failed) break;
+      } else {
+        const int buf = tj & 1;
+        const uint32_t aph = (tj >> 1) & 1;
+        if (!mbar_wait(tfull_bar(buf), aph, abort_flag, p.status)) break;
+        tc_fence_after();
+#pragma unroll 1
+        for (int j = 0; j < BN / 32; ++j) {
+          const int col0 = nt * BN + j * 32;
+          if (col0 >= p.Nc) break;  // warp-uniform
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tmem_base + lane_addr + buf * BN + j * 32, r);
+          tmem_ld_wait();
+          if (row_ok) store_row32(p, r, col0, yrow, rrow);
+        }
+        tc_fence_before();
+        mbar_arrive(tempty_bar(buf));
       }
-      tc_fence_before();
-      mbar_arrive(tempty_bar(buf));
     }
   }
 
@@ -434,9 +518,9 @@ int launch_t(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap& lo,
 }  // namespace
 
 int igemm_pick_bn(const IgemmParams& p, int precision, int num_sms) {
-  (void)precision;
   const int nc = p.Nc;
   if (nc <= 64) return 64;
+  if (precision == kPrec3xTF32) return 128;  // three BN-wide accumulators must fit TMEM
   const long long mt = (long long)((p.M + kBM - 1) / kBM) * p.batches;
   // Wide tiles halve A re-reads; use them when there are enough tiles to fill the GPU.
   if (nc >= 256 && mt * ((nc + 255) / 256) >= 2ll * num_sms) return 256;
@@ -445,11 +529,17 @@ int igemm_pick_bn(const IgemmParams& p, int precision, int num_sms) {
 
 int igemm_launch(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap& lo,
                  int precision, int bn, int num_sms, cudaStream_t st) {
+  // The kernel moves 16-byte vectors: refuse (instead of faulting on) any
+  // pointer or stride that would make one of them misaligned.
+  auto mis = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) != 0; };
+  if (!p.x || !p.y || mis(p.x) || mis(p.y) || (p.res && mis(p.res)) || (p.scale && mis(p.scale)) ||
+      (p.shift && mis(p.shift)) || p.Cs % 4 || p.Nc % 4 || p.ldy % 4 || (p.res && p.ldr % 4) ||
+      p.y_bstride % 4 || p.num_kb <= 0 || (p.batches > 1 && !p.a_off && p.M % 4))
+    return (int)cudaErrorMisalignedAddress;
 #define OB2_CASE(PR, B)                                  \
   if (precision == PR && bn == B) return launch_t<PR, B>(p, hi, lo, num_sms, st);
   OB2_CASE(kPrec3xTF32, 64)
   OB2_CASE(kPrec3xTF32, 128)
-  OB2_CASE(kPrec3xTF32, 256)
   OB2_CASE(kPrecTF32, 64)
   OB2_CASE(kPrecTF32, 128)
   OB2_CASE(kPrecTF32, 256)

@@ -22,6 +22,9 @@ struct onnxb200_handle {
   float* d_ones = nullptr;   // scratch constants
   std::string last_error;
   int64_t launches = 0;
+  // ONNXB200_DEBUG_SYNC=1: graph runs synchronize after every step and report
+  // the first step whose kernels failed (eager runs only).
+  bool debug_sync = false;
 };
 
 struct onnxb200_conv_plan {

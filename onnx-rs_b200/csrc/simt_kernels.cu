@@ -311,7 +311,8 @@ __global__ void maxpool_nhwc_idx_kernel(const float* __restrict__ x, int N, int 
 int maxpool_nhwc_launch(const float* x, int N, int C, int Cs, int H, int W, int KH, int KW, int sh,
                         int sw, int pt, int pl, int OH, int OW, float* y, long long* ind,
                         cudaStream_t st) {
-  if (!ind && C % 4 == 0 && Cs % 4 == 0) {
+  const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15) == 0;
+  if (!ind && C % 4 == 0 && Cs % 4 == 0 && aligned) {
     const long long total = (long long)N * OH * OW * (C / 4);
     if (total == 0) return 0;
     maxpool_nhwc_v4_kernel<<<grid_for(total, kBlock), kBlock, 0, st>>>(
@@ -360,7 +361,8 @@ __global__ void gap_nhwc_scalar_kernel(const float* __restrict__ x, int C, int H
 
 int gap_nhwc_launch(const float* x, int N, int C, int HW, float* y, cudaStream_t st) {
   if (N == 0 || C == 0) return 0;
-  if (C % 4 == 0) {
+  const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15) == 0;
+  if (C % 4 == 0 && aligned) {
     const int c4 = C / 4;
     const int block = c4 < 128 ? 32 * ((c4 + 31) / 32) : 128;
     dim3 grid((c4 + block - 1) / block, N);

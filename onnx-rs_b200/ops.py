@@ -140,6 +140,48 @@ class Conv(Operator):
         return [y]
 
 
+class ConvPlan:
+    """Prepared convolution (onnxb200_conv_plan_*): weights packed and BN folded once.
+
+    ``layout`` is the layout of x / residual / y at run time (NHWC runs the
+    kernel directly on the caller's buffers)."""
+
+    def __init__(self, ctx: ExecutionContext, conv: Conv, x_shape, w, bias=None, bn=None,
+                 layout=C.LAYOUT_NHWC, residual=False):
+        self.ctx = ctx
+        h = ctx.handle
+        epi = (C.EPI_BIAS if bias is not None else 0) | (C.EPI_BN if bn is not None else 0) | \
+              (C.EPI_RESIDUAL if residual else 0) | (C.EPI_RELU if conv.relu else 0)
+        self.desc = conv.desc(tuple(x_shape), tuple(w.shape), layout, epi, _prec(ctx, conv.precision),
+                              bn[4] if bn is not None else 1e-5)
+        out = C.i64_array([0] * 4)
+        h.check(C.lib().onnxb200_conv2d_output_shape(ctypes.byref(self.desc), out), "Conv")
+        n, co, oh, ow = [int(v) for v in out[:4]]
+        self.out_shape = (n, co, oh, ow) if layout == C.LAYOUT_NCHW else (n, oh, ow, co)
+        bnp = list(bn[:4]) if bn is not None else [None] * 4
+        ptr = ctypes.c_void_p()
+        h.check(C.lib().onnxb200_conv_plan_create(h.ptr, ctypes.byref(self.desc), dptr(w), dptr(bias),
+                                                  dptr(bnp[0]), dptr(bnp[1]), dptr(bnp[2]), dptr(bnp[3]),
+                                                  ctypes.byref(ptr)), "conv plan")
+        self.ptr = ptr
+
+    def run(self, x: torch.Tensor, y: torch.Tensor, residual: Optional[torch.Tensor] = None):
+        h = self.ctx.handle
+        h.check(C.lib().onnxb200_conv_plan_run(h.ptr, self.ptr, dptr(x), dptr(residual), dptr(y)), "conv plan run")
+        return y
+
+    def close(self):
+        if getattr(self, "ptr", None):
+            C.lib().onnxb200_conv_plan_destroy(self.ptr)
+            self.ptr = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 # --------------------------------------------------------------------------- MatMul / Gemm
 class MatMul(Operator):
     """MatMul (src/ops/math/matmul.rs:60-124): numpy-broadcast batched matmul."""
