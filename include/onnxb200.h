@@ -148,6 +148,30 @@ ONNXB200_API int onnxb200_conv_plan_run(onnxb200_handle* h, const onnxb200_conv_
                                         const float* x, const float* residual, float* y);
 ONNXB200_API int onnxb200_conv_plan_destroy(onnxb200_conv_plan* p);
 
+/* Conv2d + fused epilogue on NHWC device buffers that allocates no device
+ * memory.  No counterpart in the reference: it exists for callers that cannot
+ * call cudaMalloc while they run (a host framework that owns all device memory
+ * and hands in pre-sized input/output buffers, or a serving loop that cannot
+ * take an allocation or the synchronisation of a cudaFree).  Instead of a
+ * handle's growable workspace it uses one fixed array of
+ * ONNXB200_NOALLOC_SCRATCH_BYTES in device memory, defined in the library and
+ * held by every GPU that loads the library until the process exits; packed
+ * weights + epilogue vectors larger than that are rejected with
+ * ONNXB200_ERR_RESOURCE_EXHAUSTED (every ResNet-18/50 convolution fits).
+ * Runs on the current device and the given stream (NULL = legacy default
+ * stream) and returns once y is written (bounded wait); device-side failures
+ * are returned as status codes.  The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress), so make that first call
+ * before any stream capture.  All calls share the array: calls that overlap on
+ * the GPU (e.g. issued concurrently from several host threads) race on it.
+ * d->layout must be ONNXB200_LAYOUT_NHWC. */
+#define ONNXB200_NOALLOC_SCRATCH_BYTES (24u << 20)
+ONNXB200_API int onnxb200_conv2d_nhwc_noalloc(void* cuda_stream, const onnxb200_conv_desc* d,
+                                              const float* x, const float* w, const float* bias,
+                                              const float* bn_scale, const float* bn_bias,
+                                              const float* bn_mean, const float* bn_var,
+                                              const float* residual, float* y);
+
 /* ---------------------------------------------------------------- MatMul / Gemm */
 /* validate_matmul_shapes (src/ops/math/matmul.rs:401-487).  out_shape holds
  * max(a_rank, b_rank) entries. */

@@ -112,6 +112,7 @@ SIGNATURES = {
     "onnxb200_conv_plan_create": (_int, [_vp, ctypes.POINTER(ConvDesc)] + [_vp] * 6 + [ctypes.POINTER(_vp)]),
     "onnxb200_conv_plan_run": (_int, [_vp, _vp, _vp, _vp, _vp]),
     "onnxb200_conv_plan_destroy": (_int, [_vp]),
+    "onnxb200_conv2d_nhwc_noalloc": (_int, [_vp, ctypes.POINTER(ConvDesc)] + [_vp] * 9),
     "onnxb200_matmul_output_shape": (_int, [_i64p, _int, _i64p, _int, _i64p, ctypes.POINTER(_int)]),
     "onnxb200_matmul": (_int, [_vp, _vp, _i64p, _int, _vp, _i64p, _int, _vp, _int, _int, _vp]),
     "onnxb200_gemm": (_int, [_vp, _vp, _vp, _vp, _i64p, _int, _i64, _i64, _i64, _int, _int, _f32, _f32,
