@@ -294,11 +294,12 @@ def main():
         return float(t.item())
 
     ob = importlib.import_module("onnx-rs_b200")
-    per_rank = args.batch // world
+    lo, hi = ob.sharding.shard_range(args.batch, world, rank)
+    per_rank = hi - lo
     nodes, inits, ins, outs = ob.workloads.resnet50(batch=per_rank, seed=SEED)
     conv_flops_img = ob.workloads.resnet50.conv_flops_per_image
     xfull = ob.workloads.resnet_input(SEED, args.batch)
-    xs = np.ascontiguousarray(xfull[rank * per_rank:(rank + 1) * per_rank])
+    xs = np.ascontiguousarray(xfull[lo:hi])
     del xfull
 
     # one dedicated stream: the library's kernels, the L2 flush and the CUDA

@@ -12,7 +12,7 @@ from .runtime import (Handle, OnnxB200Error, ValidationError, ExecutionError, Un
 from .ops import (ExecutionContext, Operator, OperatorRegistry, Conv, ConvPlan, MatMul, Gemm, MaxPool,
                   GlobalAveragePool, Relu, Add, BatchNormalization, Flatten)
 from .graph import Graph
-from . import synth, workloads
+from . import sharding, synth, workloads
 
 LIB_PATH = _capi.LIB_PATH
 
