@@ -309,7 +309,14 @@ int conv_plan_exec_nhwc(onnxb200_handle* h, const onnxb200_conv_plan* p, const f
     q.status = h->d_status;
     q.m_tiles = (q.M + 127) / 128;
     q.n_tiles = (q.Nc + p->bn - 1) / p->bn;
-    rc = igemm_launch(q, p->tm_hi, p->tm_lo, p->prec, p->bn, h->num_sms, h->stream);
+    q.a_mode = pick_a_mode(q, p->prec);
+    CUtensorMap am{};
+    if (q.a_mode != kALoadGather) {
+      const int rows = q.a_mode == kALoadTma2d ? (int)(d.n * d.h * d.w) : (int)d.n;
+      const int er = encode_a_map(q, rows, &am);
+      if (er) return set_error(h, ONNXB200_ERR_EXECUTION, "Conv: A tensor map encode failed: " + std::to_string(er));
+    }
+    rc = igemm_launch(q, p->tm_hi, p->tm_lo, am, p->prec, p->bn, h->num_sms, h->stream);
   } else {
     rc = conv_direct_launch(x, (int)d.n, (int)d.h, (int)d.w, (int)d.c, p->cs_in, p->w_oihw,
                             (int)d.c_out, (int)d.kh, (int)d.kw, (int)d.stride_h, (int)d.stride_w,
@@ -359,7 +366,13 @@ int gemm_tc_run(onnxb200_handle* h, const GemmCall& c, const void* b_hi, const v
   if (rc) return rc;
   rc = encode_weight_map(h, &tlo, b_lo ? b_lo : b_hi, b_rows, kpad, prec, bn);
   if (rc) return rc;
-  rc = igemm_launch(q, thi, tlo, prec, bn, h->num_sms, h->stream);
+  q.a_mode = pick_a_mode(q, prec);
+  CUtensorMap am{};
+  if (q.a_mode != kALoadGather) {
+    const int er = encode_a_map(q, c.a_rows > 0 ? c.a_rows : c.M, &am);
+    if (er) return set_error(h, ONNXB200_ERR_EXECUTION, "GEMM: A tensor map encode failed: " + std::to_string(er));
+  }
+  rc = igemm_launch(q, thi, tlo, am, prec, bn, h->num_sms, h->stream);
   h->launches++;
   if (rc) return cuda_check(h, (cudaError_t)rc, "GEMM launch");
   return ONNXB200_OK;
@@ -764,6 +777,11 @@ int onnxb200_matmul(onnxb200_handle* h, const float* a, const int64_t* as, int r
   c.K = (int)K;
   c.batches = (int)nbatch;
   c.a_off = d_aoff;
+  {
+    int64_t arows = M;
+    for (auto v : ab) arows *= v;
+    c.a_rows = (int)arows;
+  }
   c.b_row = d_brow;
   c.y_bstride = M * N;
   c.y = y;

@@ -1093,6 +1093,7 @@ static int run_steps(onnxb200_graph* g, const float* const* uin, float* const* u
         c.K = gp.K;
         c.batches = gp.batches;
         c.a_off = gp.aoff_off != SIZE_MAX ? reinterpret_cast<const long long*>(g->init + gp.aoff_off) : nullptr;
+        c.a_rows = (int)(g->tensors[s.in[0]].numel() / gp.K);
         c.b_row = gp.brow_off != SIZE_MAX ? reinterpret_cast<const int*>(g->init + gp.brow_off) : nullptr;
         c.y_bstride = gp.y_bstride;
         c.y = T(s.out);

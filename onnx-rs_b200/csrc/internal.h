@@ -75,6 +75,7 @@ int conv_plan_exec_nhwc(onnxb200_handle* h, const onnxb200_conv_plan* p, const f
 struct GemmCall {
   const float* a = nullptr;  // row-major [M][K] per batch, lda == K
   int M = 0, N = 0, K = 0;
+  int a_rows = 0;            // rows of the whole A array (all batches); 0 = M
   int batches = 1;
   const long long* a_off = nullptr;  // device array or null
   const int* b_row = nullptr;        // device array or null

@@ -37,7 +37,21 @@ struct IgemmParams {
   int relu;
   int* status;             // device status word (ONNXB200_ERR_* on failure)
   int m_tiles, n_tiles;
+  // How A tiles reach shared memory: kALoadGather = per-thread 16-byte copies
+  // (any shape), kALoadTma2d = TMA tile of the [rows][Cs] matrix (1x1 stride-1
+  // convs, GEMMs), kALoadIm2col = TMA im2col over the NHWC tensor (Cs % 32 == 0).
+  int a_mode;
 };
+
+enum ALoadMode { kALoadGather = 0, kALoadTma2d = 1, kALoadIm2col = 2 };
+
+// Encodes the TMA map of the A operand for p.a_mode (x, shape and conv geometry
+// from p); returns a CUresult (0 = success).  Not needed for kALoadGather.
+int encode_a_map(const IgemmParams& p, int N, CUtensorMap* map);
+
+// Chooses the A load mode for a problem (conv geometry in p; batched GEMMs with
+// per-batch A offsets use kALoadTma2d over all rows).
+int pick_a_mode(const IgemmParams& p, int precision);
 
 // Picks BN (64/128/256) for a problem; returned value is what launch uses.
 int igemm_pick_bn(const IgemmParams& p, int precision, int num_sms);
@@ -45,7 +59,7 @@ int igemm_pick_bn(const IgemmParams& p, int precision, int num_sms);
 // Launches the tcgen05 kernel.  tm_hi / tm_lo are TMA maps over the packed
 // weights (tm_lo is only read in 3xTF32 mode).  Returns a cudaError_t.
 int igemm_launch(const IgemmParams& p, const CUtensorMap& tm_hi, const CUtensorMap& tm_lo,
-                 int precision, int bn, int num_sms, cudaStream_t stream);
+                 const CUtensorMap& tm_a, int precision, int bn, int num_sms, cudaStream_t stream);
 
 // ----------------------------------------------------------------- SIMT kernels
 // Direct convolution on CUDA cores (fp32 FFMA), any groups / channel count.
