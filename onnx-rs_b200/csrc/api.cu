@@ -78,12 +78,12 @@ int encode_weight_map(onnxb200_handle* h, CUtensorMap* map, const void* base, in
   const int esz = prec == kPrecBF16 ? 2 : 4;
   cuuint64_t dims[2] = {(cuuint64_t)kpad, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)kpad * esz};
-  cuuint32_t box[2] = {32u, (cuuint32_t)bn};
+  // one k-block of a weight row = 64 bytes (16 fp32 or 32 bf16), 64-byte swizzle
+  cuuint32_t box[2] = {(cuuint32_t)(64 / esz), (cuuint32_t)bn};
   cuuint32_t estr[2] = {1u, 1u};
   CUresult r = fn(map, prec == kPrecBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
                   2, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  prec == kPrecBF16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return set_error(h, ONNXB200_ERR_EXECUTION, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
@@ -190,8 +190,8 @@ int conv_plan_init(onnxb200_handle* h, const onnxb200_conv_desc* din, int cs_in,
   size_t off_hi = 0, off_lo = 0, off_scale = 0, off_shift = 0, off_w = 0;
   if (p->use_tc) {
     p->K = (int)(d.kh * d.kw * cs_in);
-    p->num_kb = (p->K + 31) / 32;
-    p->kpad = p->num_kb * 32;
+    p->kpad = (p->K + 31) / 32 * 32;
+    p->num_kb = p->kpad / igemm_block_k(p->prec);
     const size_t esz = p->prec == kPrecBF16 ? 2 : 4;
     const size_t wbytes = align_up((size_t)CO * p->kpad * esz);
     off_hi = need;
@@ -345,7 +345,7 @@ int gemm_tc_run(onnxb200_handle* h, const GemmCall& c, const void* b_hi, const v
   q.M = c.M;
   q.Nc = c.N;
   q.K = c.K;
-  q.num_kb = kpad / 32;
+  q.num_kb = kpad / igemm_block_k(prec);
   q.batches = c.batches;
   q.a_off = c.a_off;
   q.b_row = c.b_row;

@@ -515,431 +515,6 @@ int launch_t(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap& lo,
   return (int)cudaGetLastError();
 }
 
-// ======================================================================================
-// v2: asynchronous A pipeline, A operand in TMEM (3xTF32 and TF32).
-//
-//   warps 0-3   epilogue (as above)
-//   warps 4-7   loaders: cp.async 16-byte NHWC chunks (zero-fill = padding) into raw
-//               fp32 A stages in shared memory -- no registers held, so up to S1-1
-//               k-blocks are in flight; thread 0 also issues the TMA of the weight
-//               tiles into the same stage.  Completion: cp.async.mbarrier.arrive.noinc
-//               (128 arrivals) + the TMA's transaction bytes on s1_full[stage].
-//   warps 8-11  converters: warp 8+q owns TMEM lanes 32q..32q+31 = tile rows; each
-//               thread reads its row of the raw stage, rounds / splits it to tf32
-//               hi (and lo) and writes it to a TMEM A stage with tcgen05.st.
-//   warp 12     TMEM allocation and tcgen05.mma kind::tf32 with A from TMEM and B
-//               from shared memory (shared-memory traffic: raw A once, B).
-// TMEM: accumulators as in v1 (3xTF32: running total + two chunk accumulators),
-// then S2 A stages of 64 (hi+lo) or 32 columns.
-// ======================================================================================
-constexpr int kLoadWarp0 = 4, kConvWarp0 = 8, kMmaWarp2 = 12;
-constexpr int kThreads2 = 13 * 32;
-
-template <int PREC, int BN>
-struct Layout2 {
-  static constexpr bool kSplit = (PREC == kPrec3xTF32);
-  static constexpr int kARaw = kBM * 128;  // 128 rows x 32 fp32
-  static constexpr int kBBytes = BN * 128;
-  static constexpr int kStage = kARaw + (kSplit ? 2 : 1) * kBBytes;
-  static constexpr int kS1raw = kSmemBudget / kStage;
-  static constexpr int kS1 = kS1raw > 8 ? 8 : kS1raw;
-  static constexpr bool kPromote = kSplit;
-  static constexpr int kChunkKB = kPromote ? 2 : (1 << 30);
-  static constexpr int kAccCols = kPromote ? 3 * BN : 2 * BN;
-  static constexpr int kAStageCols = kSplit ? 64 : 32;
-  static constexpr int kS2raw = (512 - kAccCols) / kAStageCols;
-  static constexpr int kS2 = kS2raw > 4 ? 4 : kS2raw;
-  static_assert(kS2 >= 2, "TMEM too small for two A stages");
-  static constexpr int kACol0 = kAccCols;
-  static constexpr int kTmemCols = 512;
-  static constexpr int kOffA = 0;
-  static constexpr int kOffB = kS1 * kARaw;
-  static constexpr int kOffBlo = kOffB + kS1 * kBBytes;
-  static constexpr int kOffBar = kOffBlo + (kSplit ? kS1 * kBBytes : 0);
-  // s1_full[S1], s1_empty[S1], t_full[S2], t_empty[S2], acc_full[2], acc_empty[2], drain
-  static constexpr int kNumBars = 2 * kS1 + 2 * kS2 + 5;
-  static constexpr int kOffMisc = kOffBar + kNumBars * 8;
-  static constexpr int kBytes = kOffMisc + 16 + 1024;
-};
-
-template <int PREC, int BN>
-__global__ void __launch_bounds__(kThreads2, 1)
-    igemm_tc2_kernel(const __grid_constant__ IgemmParams p, const __grid_constant__ CUtensorMap tm_hi,
-                     const __grid_constant__ CUtensorMap tm_lo, const __grid_constant__ CUtensorMap tm_a) {
-  using L = Layout2<PREC, BN>;
-  constexpr int S1 = L::kS1;
-  constexpr int S2 = L::kS2;
-
-  extern __shared__ uint8_t smem_raw[];
-  const uint32_t raw_addr = smem_u32(smem_raw);
-  const uint32_t base = (raw_addr + 1023u) & ~1023u;
-  uint8_t* gbase = smem_raw + (base - raw_addr);
-  const uint32_t a_raw = base + L::kOffA, b_hi = base + L::kOffB, b_lo = base + L::kOffBlo;
-  const uint32_t bar0 = base + L::kOffBar;
-  auto s1_full = [&](int s) { return bar0 + 8u * s; };
-  auto s1_empty = [&](int s) { return bar0 + 8u * (S1 + s); };
-  auto t_full = [&](int a) { return bar0 + 8u * (2 * S1 + a); };
-  auto t_empty = [&](int a) { return bar0 + 8u * (2 * S1 + S2 + a); };
-  auto acc_full = [&](int b) { return bar0 + 8u * (2 * S1 + 2 * S2 + b); };
-  auto acc_empty = [&](int b) { return bar0 + 8u * (2 * S1 + 2 * S2 + 2 + b); };
-  const uint32_t drain_bar = bar0 + 8u * (2 * S1 + 2 * S2 + 4);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + L::kOffMisc);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + L::kOffMisc + 4);
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < S1; ++s) {
-      // gather mode: one cp.async arrival per loader thread; TMA modes: one arrival
-      // (with the transaction bytes of A and B) from the issuing thread
-      mbar_init(s1_full(s), p.a_mode == kALoadGather ? 128 : 1);
-      mbar_init(s1_empty(s), 128 + 1);
-    }
-    for (int a = 0; a < S2; ++a) {
-      mbar_init(t_full(a), 128);
-      mbar_init(t_empty(a), 1);
-    }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(acc_full(b), 1);
-      mbar_init(acc_empty(b), kEpiWarps * 32);
-    }
-    mbar_init(drain_bar, 1);
-    *abort_flag = 0;
-    fence_mbarrier_init();
-    prefetch_tmap(&tm_hi);
-    if (L::kSplit) prefetch_tmap(&tm_lo);
-    if (p.a_mode != kALoadGather) prefetch_tmap(&tm_a);
-  }
-  if (warp == kMmaWarp2) {
-    tmem_alloc(smem_u32(tmem_slot), L::kTmemCols);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
-
-  const int total_tiles = p.m_tiles * p.n_tiles * p.batches;
-  auto tile_coords = [&](int t, int& b, int& mt, int& nt) {
-    nt = t % p.n_tiles;
-    int r = t / p.n_tiles;
-    mt = r % p.m_tiles;
-    b = r / p.m_tiles;
-  };
-  const int my_tiles =
-      (blockIdx.x < total_tiles) ? (total_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-  const int total_items = my_tiles * p.num_kb;
-
-  if (warp >= kLoadWarp0 && warp < kConvWarp0) {
-    // ------------------------------------------------------------ loaders
-    const int lt = threadIdx.x - kLoadWarp0 * 32;
-    if (p.a_mode != kALoadGather) {
-      // One thread issues the A tile (TMA 2-D tile or im2col) and the B tiles
-      // of each stage; the hardware does the gather, zero fill and row wrap.
-      if (lt == 0) {
-        const int OHW = p.OH * p.OW;
-        for (int item = 0; item < total_items; ++item) {
-          const int s = item % S1;
-          if (!mbar_wait(s1_empty(s), ((item / S1) & 1) ^ 1, abort_flag, p.status)) break;
-          const int tj = item / p.num_kb;
-          const int kb = item - tj * p.num_kb;
-          int b, mt, nt;
-          tile_coords(blockIdx.x + tj * gridDim.x, b, mt, nt);
-          mbar_arrive_expect_tx(s1_full(s), L::kARaw + (L::kSplit ? 2 : 1) * L::kBBytes);
-          const int k0 = kb * 32;
-          const int tap = k0 / p.Cs;
-          const int c0 = k0 - tap * p.Cs;
-          const uint32_t dst = a_raw + s * L::kARaw;
-          if (p.a_mode == kALoadTma2d) {
-            const int row0 = (p.a_off ? (int)(p.a_off[b] / p.Cs) : 0) + mt * kBM;
-            tma_load_2d(dst, &tm_a, c0, row0, s1_full(s));
-          } else {
-            const int m0 = mt * kBM;
-            const int n0 = m0 / OHW;
-            const int rem = m0 - n0 * OHW;
-            const int oh0 = rem / p.OW;
-            const int ow0 = rem - oh0 * p.OW;
-            const int r = tap / p.KW;
-            const int q = tap - r * p.KW;
-            tma_load_im2col_4d(dst, &tm_a, c0, ow0 * p.sw - p.pw, oh0 * p.sh - p.ph, n0,
-                               (uint16_t)(q * p.dw), (uint16_t)(r * p.dh), s1_full(s));
-          }
-          const int brow = nt * BN + (p.b_row ? p.b_row[b] : 0);
-          tma_load_2d(b_hi + s * L::kBBytes, &tm_hi, k0, brow, s1_full(s));
-          if (L::kSplit) tma_load_2d(b_lo + s * L::kBBytes, &tm_lo, k0, brow, s1_full(s));
-        }
-      }
-    } else {
-    const int chunk = lt & 7;
-    const int rslot = lt >> 3;
-    int pix[8], ih0[8], iw0[8];
-    const float* xb = p.x;
-    int cur_tile = -1;
-    const int OHW = p.OH * p.OW;
-    for (int item = 0; item < total_items; ++item) {
-      const int s = item % S1;
-      if (!mbar_wait(s1_empty(s), ((item / S1) & 1) ^ 1, abort_flag, p.status)) break;
-      const int tj = item / p.num_kb;
-      const int kb = item - tj * p.num_kb;
-      int b, mt, nt;
-      tile_coords(blockIdx.x + tj * gridDim.x, b, mt, nt);
-      if (tj != cur_tile) {
-        cur_tile = tj;
-        xb = p.x + (p.a_off ? p.a_off[b] : 0ll);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int m = mt * kBM + rslot + 16 * i;
-          if (m < p.M) {
-            const int n = m / OHW;
-            const int rem = m - n * OHW;
-            const int oh = rem / p.OW;
-            const int ow = rem - oh * p.OW;
-            pix[i] = n * p.Hin * p.Win;
-            ih0[i] = oh * p.sh - p.ph;
-            iw0[i] = ow * p.sw - p.pw;
-          } else {
-            pix[i] = 0;
-            ih0[i] = -(1 << 28);
-            iw0[i] = 0;
-          }
-        }
-      }
-      if (lt == 0) {
-        const int brow = nt * BN + (p.b_row ? p.b_row[b] : 0);
-        mbar_expect_tx(s1_full(s), (L::kSplit ? 2 : 1) * L::kBBytes);
-        tma_load_2d(b_hi + s * L::kBBytes, &tm_hi, kb * 32, brow, s1_full(s));
-        if (L::kSplit) tma_load_2d(b_lo + s * L::kBBytes, &tm_lo, kb * 32, brow, s1_full(s));
-      }
-      const int k = kb * 32 + chunk * 4;
-      int dy = 0, dx = 0, ci = 0;
-      const bool kval = k < p.K;
-      if (kval) {
-        const int tap = k / p.Cs;
-        ci = k - tap * p.Cs;
-        const int r = tap / p.KW;
-        dy = r * p.dh;
-        dx = (tap - r * p.KW) * p.dw;
-      }
-      const uint32_t stage = a_raw + s * L::kARaw;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int row = rslot + 16 * i;
-        const int ih = ih0[i] + dy, iw = iw0[i] + dx;
-        const bool ok = kval && (unsigned)ih < (unsigned)p.Hin && (unsigned)iw < (unsigned)p.Win;
-        const float* src = ok ? xb + ((long long)pix[i] + (long long)ih * p.Win + iw) * p.Cs + ci : p.x;
-        cp_async_16(stage + swz_off(row, chunk, 128), src, ok ? 16u : 0u);
-      }
-      cp_async_arrive_noinc(s1_full(s));
-    }
-    cp_async_wait_all();
-    }
-  } else if (warp >= kConvWarp0 && warp < kMmaWarp2) {
-    // ------------------------------------------------------------ converters
-    const int q = warp - kConvWarp0;  // TMEM lane quadrant
-    const int row = q * 32 + lane;
-    const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
-    for (int item = 0; item < total_items; ++item) {
-      const int s = item % S1;
-      const int a = item % S2;
-      if (!mbar_wait(s1_full(s), (item / S1) & 1, abort_flag, p.status)) break;
-      const uint32_t rbase = a_raw + s * L::kARaw + row * 128;
-      float v[32];
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const float4 f = ld_shared_f4(rbase + ((c ^ (row & 7)) << 4));
-        v[4 * c] = f.x;
-        v[4 * c + 1] = f.y;
-        v[4 * c + 2] = f.z;
-        v[4 * c + 3] = f.w;
-      }
-      mbar_arrive(s1_empty(s));  // raw A of this stage consumed
-      uint32_t hi[32];
-#pragma unroll
-      for (int e = 0; e < 32; ++e) hi[e] = __float_as_uint(to_tf32(v[e]));
-      if (!mbar_wait(t_empty(a), ((item / S2) & 1) ^ 1, abort_flag, p.status)) break;
-      tc_fence_after();
-      const uint32_t acol = tmem_base + lane_addr + L::kACol0 + a * L::kAStageCols;
-      tmem_st_32x32b_x32(acol, hi);
-      if constexpr (L::kSplit) {
-        uint32_t lo[32];
-#pragma unroll
-        for (int e = 0; e < 32; ++e) lo[e] = __float_as_uint(to_tf32(v[e] - __uint_as_float(hi[e])));
-        tmem_st_32x32b_x32(acol + 32, lo);
-      }
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(t_full(a));
-    }
-  } else if (warp == kMmaWarp2) {
-    // ------------------------------------------------------------ MMA issuer
-    constexpr uint32_t idesc = make_idesc(2, kBM, BN);
-    int item = 0;
-    bool issued = false;
-    uint32_t cc = 0;
-    for (int tj = 0; tj < my_tiles; ++tj) {
-      const int buf = tj & 1;
-      uint32_t d_tmem = tmem_base + buf * BN;
-      int cb = 0;
-      if constexpr (!L::kPromote) {
-        if (!mbar_wait(acc_empty(buf), ((tj >> 1) & 1) ^ 1, abort_flag, p.status)) break;
-        tc_fence_after();
-      }
-      bool failed = false;
-      for (int kb = 0; kb < p.num_kb; ++kb, ++item) {
-        const int s = item % S1;
-        const int a = item % S2;
-        const int kin = kb % L::kChunkKB;
-        if constexpr (L::kPromote) {
-          if (kin == 0) {
-            cb = cc & 1;
-            if (!mbar_wait(acc_empty(cb), ((cc >> 1) & 1) ^ 1, abort_flag, p.status)) {
-              failed = true;
-              break;
-            }
-            tc_fence_after();
-            d_tmem = tmem_base + BN * (1 + cb);
-          }
-        }
-        if (!mbar_wait(t_full(a), (item / S2) & 1, abort_flag, p.status) ||
-            !mbar_wait(s1_full(s), (item / S1) & 1, abort_flag, p.status)) {
-          failed = true;
-          break;
-        }
-        tc_fence_after();
-        if (lane == 0) {
-          const uint32_t ahi = tmem_base + L::kACol0 + a * L::kAStageCols;
-          const uint64_t dbh = smem_desc_sw128(b_hi + s * L::kBBytes);
-          uint64_t dbl = 0;
-          if constexpr (L::kSplit) dbl = smem_desc_sw128(b_lo + s * L::kBBytes);
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint32_t acc = ((L::kPromote ? kin : kb) | kk) ? 1u : 0u;
-            tc_mma_tf32_ts(d_tmem, ahi + kk * 8, dbh + (uint64_t)(kk * 2), idesc, acc);
-            if constexpr (L::kSplit) {
-              tc_mma_tf32_ts(d_tmem, ahi + kk * 8, dbl + (uint64_t)(kk * 2), idesc, 1u);
-              tc_mma_tf32_ts(d_tmem, ahi + 32 + kk * 8, dbh + (uint64_t)(kk * 2), idesc, 1u);
-            }
-          }
-          tc_commit(s1_empty(s));
-          tc_commit(t_empty(a));
-          issued = true;
-        }
-        if constexpr (L::kPromote) {
-          if (kin == L::kChunkKB - 1 || kb == p.num_kb - 1) {
-            if (lane == 0) tc_commit(acc_full(cb));
-            ++cc;
-          }
-        }
-        __syncwarp();
-      }
-      if (failed) break;
-      if constexpr (!L::kPromote) {
-        if (lane == 0) tc_commit(acc_full(buf));
-      }
-      __syncwarp();
-    }
-    if (lane == 0 && issued) {
-      tc_commit(drain_bar);
-      volatile int no_abort = 0;
-      mbar_wait(drain_bar, 0, &no_abort, p.status);
-    }
-    __syncwarp();
-  } else {
-    // ------------------------------------------------------------ epilogue
-    const int row_in_tile = warp * 32 + lane;
-    const uint32_t lane_addr = (uint32_t)(warp * 32) << 16;
-    uint32_t cc = 0;
-    for (int tj = 0; tj < my_tiles; ++tj) {
-      int b, mt, nt;
-      tile_coords(blockIdx.x + tj * gridDim.x, b, mt, nt);
-      const int m = mt * kBM + row_in_tile;
-      const bool row_ok = m < p.M;
-      float* yrow = p.y + (long long)b * p.y_bstride + (long long)m * p.ldy;
-      const float* rrow =
-          p.res ? p.res + (long long)b * p.y_bstride + (long long)m * p.ldr : nullptr;
-      if constexpr (L::kPromote) {
-        const int nch = (p.num_kb + L::kChunkKB - 1) / L::kChunkKB;
-        bool failed = false;
-        for (int ch = 0; ch < nch; ++ch, ++cc) {
-          const int cb = cc & 1;
-          if (!mbar_wait(acc_full(cb), (cc >> 1) & 1, abort_flag, p.status)) {
-            failed = true;
-            break;
-          }
-          tc_fence_after();
-          const bool last = ch == nch - 1;
-#pragma unroll 1
-          for (int j = 0; j < BN / 32; ++j) {
-            const int col0 = nt * BN + j * 32;
-            if (col0 >= p.Nc) break;  // warp-uniform
-            uint32_t r[32];
-            tmem_ld_32x32b_x32(tmem_base + lane_addr + BN * (1 + cb) + j * 32, r);
-            if (ch > 0) {
-              uint32_t t[32];
-              tmem_ld_32x32b_x32(tmem_base + lane_addr + j * 32, t);
-              tmem_ld_wait();
-#pragma unroll
-              for (int e = 0; e < 32; ++e)
-                r[e] = __float_as_uint(__uint_as_float(t[e]) + __uint_as_float(r[e]));
-            } else {
-              tmem_ld_wait();
-            }
-            if (!last)
-              tmem_st_32x32b_x32(tmem_base + lane_addr + j * 32, r);
-            else if (row_ok)
-              store_row32(p, r, col0, yrow, rrow);
-          }
-          if (!last) tmem_st_wait();
-          tc_fence_before();
-          mbar_arrive(acc_empty(cb));
-        }
-        if (failed) break;
-      } else {
-        const int buf = tj & 1;
-        if (!mbar_wait(acc_full(buf), (tj >> 1) & 1, abort_flag, p.status)) break;
-        tc_fence_after();
-#pragma unroll 1
-        for (int j = 0; j < BN / 32; ++j) {
-          const int col0 = nt * BN + j * 32;
-          if (col0 >= p.Nc) break;
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(tmem_base + lane_addr + buf * BN + j * 32, r);
-          tmem_ld_wait();
-          if (row_ok) store_row32(p, r, col0, yrow, rrow);
-        }
-        tc_fence_before();
-        mbar_arrive(acc_empty(buf));
-      }
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == kMmaWarp2) {
-    tc_fence_after();
-    tmem_dealloc(tmem_base, L::kTmemCols);
-  }
-}
-
-template <int PREC, int BN>
-int launch2_t(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap& lo,
-              const CUtensorMap& am, int num_sms, cudaStream_t st) {
-  using L = Layout2<PREC, BN>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(igemm_tc2_kernel<PREC, BN>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
-    if (e != cudaSuccess) return (int)e;
-    attr_set = true;
-  }
-  const int total = p.m_tiles * p.n_tiles * p.batches;
-  const int grid = total < num_sms ? total : num_sms;
-  if (grid <= 0) return 0;
-  igemm_tc2_kernel<PREC, BN><<<grid, kThreads2, L::kBytes, st>>>(p, hi, lo, am);
-  return (int)cudaGetLastError();
-}
-
 }  // namespace
 
 int igemm_pick_bn(const IgemmParams& p, int precision, int num_sms) {
@@ -955,7 +530,7 @@ int igemm_pick_bn(const IgemmParams& p, int precision, int num_sms) {
 
 int igemm_launch(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap& lo,
                  const CUtensorMap& am, int precision, int bn, int num_sms, cudaStream_t st) {
-  if (p.a_mode != kALoadGather && (precision == kPrecBF16 || p.Cs % 32 != 0))
+  if (p.a_mode != kALoadGather && (precision == kPrecBF16 || p.Cs % 16 != 0))
     return (int)cudaErrorInvalidValue;
   // The kernel moves 16-byte vectors: refuse (instead of faulting on) any
   // pointer or stride that would make one of them misaligned.
@@ -964,13 +539,8 @@ int igemm_launch(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap&
       (p.shift && mis(p.shift)) || p.Cs % 4 || p.Nc % 4 || p.ldy % 4 || (p.res && p.ldr % 4) ||
       p.y_bstride % 4 || p.num_kb <= 0 || (p.batches > 1 && !p.a_off && p.M % 4))
     return (int)cudaErrorMisalignedAddress;
-#define OB2_CASE2(PR, B)                                 \
-  if (precision == PR && bn == B) return launch2_t<PR, B>(p, hi, lo, am, num_sms, st);
-  OB2_CASE2(kPrec3xTF32, 64)
-  OB2_CASE2(kPrec3xTF32, 128)
-  OB2_CASE2(kPrecTF32, 64)
-  OB2_CASE2(kPrecTF32, 128)
-#undef OB2_CASE2
+  if (precision == kPrec3xTF32 || precision == kPrecTF32)
+    return igemm3_launch(p, hi, lo, am, precision, bn, num_sms, st);
 #define OB2_CASE(PR, B)                                  \
   if (precision == PR && bn == B) return launch_t<PR, B>(p, hi, lo, num_sms, st);
   OB2_CASE(kPrecBF16, 64)
@@ -981,7 +551,8 @@ int igemm_launch(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap&
 }
 
 int pick_a_mode(const IgemmParams& p, int precision) {
-  if (precision == kPrecBF16 || p.Cs % 32 != 0 || p.K % 32 != 0) return kALoadGather;
+  // TMA boxes carry 16 channels (64 bytes) of one filter tap per k-block
+  if (precision == kPrecBF16 || p.Cs % 16 != 0 || p.K % 16 != 0) return kALoadGather;
   const bool single_tap = p.K == p.Cs;
   if (single_tap && p.sh == 1 && p.sw == 1 && p.ph == 0 && p.pw == 0 && p.OH == p.Hin &&
       p.OW == p.Win)
@@ -1027,10 +598,10 @@ int encode_a_map(const IgemmParams& p, int n, CUtensorMap* map) {
     // n = number of rows of the [rows][Cs] matrix (pixels of the batch, or all A rows)
     cuuint64_t dims[2] = {(cuuint64_t)p.Cs, (cuuint64_t)n};
     cuuint64_t strides[1] = {(cuuint64_t)p.Cs * 4};
-    cuuint32_t box[2] = {32u, (cuuint32_t)kBM};
+    cuuint32_t box[2] = {16u, (cuuint32_t)kBM};
     cuuint32_t es[2] = {1u, 1u};
     return (int)fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, es,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   }
   static EncodeIm2colFn fn = reinterpret_cast<EncodeIm2colFn>(driver_fn("cuTensorMapEncodeIm2col"));
@@ -1044,8 +615,8 @@ int encode_a_map(const IgemmParams& p, int n, CUtensorMap* map) {
   int lower[2] = {-p.pw, -p.ph};
   int upper[2] = {(p.OW - 1) * p.sw - p.pw - (p.Win - 1), (p.OH - 1) * p.sh - p.ph - (p.Hin - 1)};
   cuuint32_t es[4] = {1u, (cuuint32_t)p.sw, (cuuint32_t)p.sh, 1u};
-  return (int)fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, dims, strides, lower, upper, 32u,
-                 (cuuint32_t)kBM, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+  return (int)fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, dims, strides, lower, upper, 16u,
+                 (cuuint32_t)kBM, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
 

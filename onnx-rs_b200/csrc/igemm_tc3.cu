@@ -1,0 +1,619 @@
+// tcgen05 implicit-GEMM kernel for the fp32-input modes (3xTF32 and TF32):
+// convolution without an im2col buffer, and batched broadcast GEMM.
+//
+// Replaces the reference's compute_conv2d_im2col + im2col_2d
+// (src/ops/nn/conv.rs:1142-1368), the direct 1x1 path (conv.rs:849-935),
+// compute_matmul's per-batch sgemm (src/ops/math/matmul.rs:124-279) and
+// compute_gemm (src/ops/math/gemm.rs:172-291).
+//
+// Persistent, warp-specialised, one 416-thread CTA per SM.  Tile 128 x BN
+// (BN = 64 or 128), k-blocks of 16 fp32 (64-byte swizzled rows).
+//   warps 0-3   epilogue: TMEM -> registers, per-channel scale/shift (bias, folded
+//               BatchNormalization), residual, Relu; each 128 x 32 block is staged in
+//               shared memory and written with one TMA store (the hardware clips rows
+//               >= M and columns >= N); residual blocks arrive by TMA load.
+//   warps 4-7   A loaders.  TMA modes: one thread issues, per k-block, the A tile
+//               (2-D tile of the [pixels][channels] matrix for 1x1 stride-1 convs and
+//               GEMMs, or an im2col box for k x k convs: the hardware walks 128 output
+//               pixels across rows and images, zero fill = padding) and the weight
+//               tiles.  Gather mode (channel counts not a multiple of 16, e.g. the RGB
+//               stem): 16-byte cp.async copies with zero fill.
+//   warps 8-11  converters: warp 8+q owns TMEM lanes 32q..32q+31 (= tile rows); each
+//               thread reads its row of the raw fp32 stage, rounds (TF32) or splits
+//               (3xTF32: hi = rna(v), lo = rna(v - hi)) and writes it to a TMEM A stage.
+//   warp 12     TMEM allocation and single-thread tcgen05.mma (kind::tf32, A from
+//               TMEM, B from shared memory).
+// 3xTF32: a*b ~= a_hi*b_hi + a_hi*b_lo + a_lo*b_hi (Ootomo & Yokota, 2022).  The
+// tensor core adds into its fp32 accumulator with truncation, so each TMEM
+// accumulator sums only 4 k-blocks (24 MMAs) and the epilogue warps fold these
+// chunks into a running total with round-to-nearest fp32 adds.
+//
+// Every wait is bounded (kWaitTimeoutNs); on expiry the kernel records
+// ONNXB200_ERR_TIMEOUT in the status word and winds down.  The epilogue warps
+// take every abort decision together (barrier AND-reduction), so none of them is
+// ever left waiting at a named barrier.
+#include <cuda_runtime.h>
+
+#include "kernels.h"
+#include "ptx.cuh"
+
+namespace ob2 {
+
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 16;  // fp32 K elements per k-block
+constexpr int kEpiThreads = 128;
+constexpr int kLoadWarp0 = 4, kConvWarp0 = 8, kMmaWarp = 12;
+constexpr int kThreads = 13 * 32;
+constexpr int kSmemBudget = 220 * 1024;
+constexpr int kEpiTile = kBM * 32 * 4;  // one 128 x 32 fp32 staging tile (16 KB)
+
+template <int PREC, int BN>
+struct Layout {
+  static constexpr bool kSplit = (PREC == kPrec3xTF32);
+  static constexpr int kARaw = kBM * kBK * 4;   // 8 KB
+  static constexpr int kBBytes = BN * kBK * 4;  // one B operand (hi or lo)
+  static constexpr int kStage = kARaw + (kSplit ? 2 : 1) * kBBytes;
+  static constexpr int kEpiBytes = 4 * kEpiTile;  // out[2] + res[2]
+  static constexpr int kS1raw = (kSmemBudget - kEpiBytes) / kStage;
+  static constexpr int kS1 = kS1raw > 8 ? 8 : kS1raw;
+  static constexpr bool kPromote = kSplit;
+  static constexpr int kChunkKB = kPromote ? 8 : (1 << 30);  // 48 MMAs per chunk
+  static constexpr int kAccCols = kPromote ? 3 * BN : 2 * BN;
+  static constexpr int kAStageCols = kSplit ? 2 * kBK : kBK;
+  static constexpr int kS2raw = (512 - kAccCols) / kAStageCols;
+  static constexpr int kS2 = kS2raw > 4 ? 4 : kS2raw;
+  static_assert(kS2 >= 2, "TMEM too small for two A stages");
+  static_assert(kS1 >= 3, "shared memory too small");
+  static constexpr int kACol0 = kAccCols;
+  static constexpr int kTmemCols = 512;
+  static constexpr int kOffOut = 0;                     // out[2]  (1024-aligned tiles)
+  static constexpr int kOffRes = 2 * kEpiTile;          // res[2]
+  static constexpr int kOffA = 4 * kEpiTile;            // raw A stages
+  static constexpr int kOffB = kOffA + kS1 * kARaw;     // B hi stages
+  static constexpr int kOffBlo = kOffB + kS1 * kBBytes;  // B lo stages
+  static constexpr int kOffBar = kOffBlo + (kSplit ? kS1 * kBBytes : 0);
+  // s1_full[S1], s1_empty[S1], t_full[S2], t_empty[S2], acc_full[2], acc_empty[2],
+  // res_full[2], drain
+  static constexpr int kNumBars = 2 * kS1 + 2 * kS2 + 7;
+  static constexpr int kOffMisc = kOffBar + kNumBars * 8;
+  static constexpr int kBytes = kOffMisc + 16 + 1024;
+};
+
+// 64-byte-swizzle layout of a [rows][16 fp32] tile: 16-byte chunk c of row r.
+__device__ __forceinline__ uint32_t swz64(int r, int c) { return r * 64 + ((c ^ ((r >> 1) & 3)) << 4); }
+// 128-byte-swizzle layout of a [rows][32 fp32] tile.
+__device__ __forceinline__ uint32_t swz128(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
+
+__device__ __forceinline__ void sts_v4(uint32_t addr, float a, float b, float c, float d) {
+  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
+// K-major operand, 64-byte swizzle: 8-row atoms of 512 bytes.
+__device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(1u) << 16;
+  d |= static_cast<uint64_t>(512u >> 4) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(4u) << 61;  // SWIZZLE_64B
+  return d;
+}
+
+template <int PREC, int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    igemm_tc3_kernel(const __grid_constant__ IgemmParams p, const __grid_constant__ CUtensorMap tm_hi,
+                     const __grid_constant__ CUtensorMap tm_lo, const __grid_constant__ CUtensorMap tm_a,
+                     const __grid_constant__ CUtensorMap tm_y, const __grid_constant__ CUtensorMap tm_res) {
+  using L = Layout<PREC, BN>;
+  constexpr int S1 = L::kS1;
+  constexpr int S2 = L::kS2;
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw_addr);
+  const uint32_t out_st = base + L::kOffOut, res_st = base + L::kOffRes;
+  const uint32_t a_raw = base + L::kOffA, b_hi = base + L::kOffB, b_lo = base + L::kOffBlo;
+  const uint32_t bar0 = base + L::kOffBar;
+  auto s1_full = [&](int s) { return bar0 + 8u * s; };
+  auto s1_empty = [&](int s) { return bar0 + 8u * (S1 + s); };
+  auto t_full = [&](int a) { return bar0 + 8u * (2 * S1 + a); };
+  auto t_empty = [&](int a) { return bar0 + 8u * (2 * S1 + S2 + a); };
+  auto acc_full = [&](int b) { return bar0 + 8u * (2 * S1 + 2 * S2 + b); };
+  auto acc_empty = [&](int b) { return bar0 + 8u * (2 * S1 + 2 * S2 + 2 + b); };
+  auto res_full = [&](int b) { return bar0 + 8u * (2 * S1 + 2 * S2 + 4 + b); };
+  const uint32_t drain_bar = bar0 + 8u * (2 * S1 + 2 * S2 + 6);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + L::kOffMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + L::kOffMisc + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S1; ++s) {
+      // gather mode: one cp.async arrival per loader thread; TMA modes: one
+      // arrival (with the transaction bytes of A and B) from the issuing thread
+      mbar_init(s1_full(s), p.a_mode == kALoadGather ? 128 : 1);
+      mbar_init(s1_empty(s), 128 + 1);  // converters + the MMA commit
+    }
+    for (int a = 0; a < S2; ++a) {
+      mbar_init(t_full(a), 128);
+      mbar_init(t_empty(a), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(acc_full(b), 1);
+      mbar_init(acc_empty(b), kEpiThreads);
+      mbar_init(res_full(b), 1);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+    prefetch_tmap(&tm_hi);
+    if (L::kSplit) prefetch_tmap(&tm_lo);
+    if (p.a_mode != kALoadGather) prefetch_tmap(&tm_a);
+    prefetch_tmap(&tm_y);
+    if (p.res) prefetch_tmap(&tm_res);
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(smem_u32(tmem_slot), L::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int total_tiles = p.m_tiles * p.n_tiles * p.batches;
+  // tile t -> (batch, m-tile, n-tile), n fastest: CTAs running together share
+  // the A tiles through L2
+  auto tile_coords = [&](int t, int& b, int& mt, int& nt) {
+    nt = t % p.n_tiles;
+    const int r = t / p.n_tiles;
+    mt = r % p.m_tiles;
+    b = r / p.m_tiles;
+  };
+  const int my_tiles =
+      (blockIdx.x < total_tiles) ? (total_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int total_items = my_tiles * p.num_kb;
+
+  if (warp >= kLoadWarp0 && warp < kConvWarp0) {
+    // ------------------------------------------------------------ loaders
+    const int lt = threadIdx.x - kLoadWarp0 * 32;
+    if (p.a_mode != kALoadGather) {
+      // lane 0 of each of the 4 loader warps issues every 4th stage: the TMA
+      // issue path of one thread is slower than the MMAs of one stage
+      if (lane == 0) {
+        const int OHW = p.OH * p.OW;
+        for (int item = warp - kLoadWarp0; item < total_items; item += 4) {
+          const int s = item % S1;
+          if (!mbar_wait(s1_empty(s), ((item / S1) & 1) ^ 1, abort_flag, p.status)) break;
+          const int tj = item / p.num_kb;
+          const int kb = item - tj * p.num_kb;
+          int b, mt, nt;
+          tile_coords(blockIdx.x + tj * gridDim.x, b, mt, nt);
+          mbar_arrive_expect_tx(s1_full(s), L::kARaw + (L::kSplit ? 2 : 1) * L::kBBytes);
+          const int k0 = kb * kBK;
+          const int tap = k0 / p.Cs;
+          const int c0 = k0 - tap * p.Cs;
+          const uint32_t dst = a_raw + s * L::kARaw;
+          if (p.a_mode == kALoadTma2d) {
+            const int row0 = (p.a_off ? (int)(p.a_off[b] / p.Cs) : 0) + mt * kBM;
+            tma_load_2d(dst, &tm_a, c0, row0, s1_full(s));
+          } else {
+            const int m0 = mt * kBM;
+            const int n0 = m0 / OHW;
+            const int rem = m0 - n0 * OHW;
+            const int oh0 = rem / p.OW;
+            const int ow0 = rem - oh0 * p.OW;
+            const int r = tap / p.KW;
+            const int q = tap - r * p.KW;
+            tma_load_im2col_4d(dst, &tm_a, c0, ow0 * p.sw - p.pw, oh0 * p.sh - p.ph, n0,
+                               (uint16_t)(q * p.dw), (uint16_t)(r * p.dh), s1_full(s));
+          }
+          const int brow = nt * BN + (p.b_row ? p.b_row[b] : 0);
+          tma_load_2d(b_hi + s * L::kBBytes, &tm_hi, k0, brow, s1_full(s));
+          if (L::kSplit) tma_load_2d(b_lo + s * L::kBBytes, &tm_lo, k0, brow, s1_full(s));
+        }
+      }
+    } else {
+      // thread -> (16-byte chunk c of 4 per row, rows rslot + 32 i)
+      const int chunk = lt & 3;
+      const int rslot = lt >> 2;
+      int pix[4], ih0[4], iw0[4];
+      const float* xb = p.x;
+      int cur_tile = -1;
+      const int OHW = p.OH * p.OW;
+      for (int item = 0; item < total_items; ++item) {
+        const int s = item % S1;
+        if (!mbar_wait(s1_empty(s), ((item / S1) & 1) ^ 1, abort_flag, p.status)) break;
+        const int tj = item / p.num_kb;
+        const int kb = item - tj * p.num_kb;
+        int b, mt, nt;
+        tile_coords(blockIdx.x + tj * gridDim.x, b, mt, nt);
+        if (tj != cur_tile) {
+          cur_tile = tj;
+          xb = p.x + (p.a_off ? p.a_off[b] : 0ll);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int m = mt * kBM + rslot + 32 * i;
+            if (m < p.M) {
+              const int n = m / OHW;
+              const int rem = m - n * OHW;
+              const int oh = rem / p.OW;
+              const int ow = rem - oh * p.OW;
+              pix[i] = n * p.Hin * p.Win;
+              ih0[i] = oh * p.sh - p.ph;
+              iw0[i] = ow * p.sw - p.pw;
+            } else {
+              pix[i] = 0;
+              ih0[i] = -(1 << 28);
+              iw0[i] = 0;
+            }
+          }
+        }
+        if (lt == 0) {
+          const int brow = nt * BN + (p.b_row ? p.b_row[b] : 0);
+          mbar_expect_tx(s1_full(s), (L::kSplit ? 2 : 1) * L::kBBytes);
+          tma_load_2d(b_hi + s * L::kBBytes, &tm_hi, kb * kBK, brow, s1_full(s));
+          if (L::kSplit) tma_load_2d(b_lo + s * L::kBBytes, &tm_lo, kb * kBK, brow, s1_full(s));
+        }
+        const int k = kb * kBK + chunk * 4;
+        int dy = 0, dx = 0, ci = 0;
+        const bool kval = k < p.K;
+        if (kval) {
+          const int tap = k / p.Cs;
+          ci = k - tap * p.Cs;
+          const int r = tap / p.KW;
+          dy = r * p.dh;
+          dx = (tap - r * p.KW) * p.dw;
+        }
+        const uint32_t stage = a_raw + s * L::kARaw;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int row = rslot + 32 * i;
+          const int ih = ih0[i] + dy, iw = iw0[i] + dx;
+          const bool ok = kval && (unsigned)ih < (unsigned)p.Hin && (unsigned)iw < (unsigned)p.Win;
+          const float* src =
+              ok ? xb + ((long long)pix[i] + (long long)ih * p.Win + iw) * p.Cs + ci : p.x;
+          cp_async_16(stage + swz64(row, chunk), src, ok ? 16u : 0u);
+        }
+        cp_async_arrive_noinc(s1_full(s));
+      }
+      cp_async_wait_all();
+    }
+  } else if (warp >= kConvWarp0 && warp < kMmaWarp) {
+    // ------------------------------------------------------------ converters
+    const int q = warp - kConvWarp0;  // TMEM lane quadrant
+    const int row = q * 32 + lane;
+    const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+    for (int item = 0; item < total_items; ++item) {
+      const int s = item % S1;
+      const int a = item % S2;
+      if (!mbar_wait(s1_full(s), (item / S1) & 1, abort_flag, p.status)) break;
+      const uint32_t rbase = a_raw + s * L::kARaw;
+      float v[16];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const float4 f = ld_shared_f4(rbase + swz64(row, c));
+        v[4 * c] = f.x;
+        v[4 * c + 1] = f.y;
+        v[4 * c + 2] = f.z;
+        v[4 * c + 3] = f.w;
+      }
+      mbar_arrive(s1_empty(s));  // raw A of this stage consumed
+      uint32_t hi[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) hi[e] = __float_as_uint(to_tf32(v[e]));
+      if (!mbar_wait(t_empty(a), ((item / S2) & 1) ^ 1, abort_flag, p.status)) break;
+      tc_fence_after();
+      const uint32_t acol = tmem_base + lane_addr + L::kACol0 + a * L::kAStageCols;
+      tmem_st_32x32b_x16(acol, hi);
+      if constexpr (L::kSplit) {
+        uint32_t lo[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) lo[e] = __float_as_uint(to_tf32(v[e] - __uint_as_float(hi[e])));
+        tmem_st_32x32b_x16(acol + kBK, lo);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(t_full(a));
+    }
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------ MMA issuer
+    constexpr uint32_t idesc = make_idesc(2, kBM, BN);
+    int item = 0;
+    bool issued = false;
+    uint32_t cc = 0;
+    for (int tj = 0; tj < my_tiles; ++tj) {
+      const int buf = tj & 1;
+      uint32_t d_tmem = tmem_base + buf * BN;
+      int cb = 0;
+      if constexpr (!L::kPromote) {
+        if (!mbar_wait(acc_empty(buf), ((tj >> 1) & 1) ^ 1, abort_flag, p.status)) break;
+        tc_fence_after();
+      }
+      bool failed = false;
+      for (int kb = 0; kb < p.num_kb; ++kb, ++item) {
+        const int s = item % S1;
+        const int a = item % S2;
+        const int kin = kb % L::kChunkKB;
+        if constexpr (L::kPromote) {
+          if (kin == 0) {
+            cb = cc & 1;
+            if (!mbar_wait(acc_empty(cb), ((cc >> 1) & 1) ^ 1, abort_flag, p.status)) {
+              failed = true;
+              break;
+            }
+            tc_fence_after();
+            d_tmem = tmem_base + BN * (1 + cb);
+          }
+        }
+        if (!mbar_wait(t_full(a), (item / S2) & 1, abort_flag, p.status) ||
+            !mbar_wait(s1_full(s), (item / S1) & 1, abort_flag, p.status)) {
+          failed = true;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t ahi = tmem_base + L::kACol0 + a * L::kAStageCols;
+          const uint64_t dbh = smem_desc_sw64(b_hi + s * L::kBBytes);
+          uint64_t dbl = 0;
+          if constexpr (L::kSplit) dbl = smem_desc_sw64(b_lo + s * L::kBBytes);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 8; ++kk) {
+            const uint32_t acc = ((L::kPromote ? kin : kb) | kk) ? 1u : 0u;
+            tc_mma_tf32_ts(d_tmem, ahi + kk * 8, dbh + (uint64_t)(kk * 2), idesc, acc);
+            if constexpr (L::kSplit) {
+              tc_mma_tf32_ts(d_tmem, ahi + kk * 8, dbl + (uint64_t)(kk * 2), idesc, 1u);
+              tc_mma_tf32_ts(d_tmem, ahi + kBK + kk * 8, dbh + (uint64_t)(kk * 2), idesc, 1u);
+            }
+          }
+          tc_commit(s1_empty(s));
+          tc_commit(t_empty(a));
+          issued = true;
+        }
+        if constexpr (L::kPromote) {
+          if (kin == L::kChunkKB - 1 || kb == p.num_kb - 1) {
+            if (lane == 0) tc_commit(acc_full(cb));
+            ++cc;
+          }
+        }
+        __syncwarp();
+      }
+      if (failed) break;
+      if constexpr (!L::kPromote) {
+        if (lane == 0) tc_commit(acc_full(buf));
+      }
+      __syncwarp();
+    }
+    // every MMA issued by this thread completes before TMEM is freed
+    if (lane == 0 && issued) {
+      tc_commit(drain_bar);
+      volatile int no_abort = 0;
+      mbar_wait(drain_bar, 0, &no_abort, p.status);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int et = threadIdx.x;  // 0..127 = tile row
+    const uint32_t lane_addr = (uint32_t)(warp * 32) << 16;
+    uint32_t cc = 0;   // accumulator chunks consumed
+    uint32_t grp = 0;  // 32-column output groups produced (staging buffer = grp & 1)
+    bool ok = true;
+    // thread 0: residual loads issued but not yet waited for (per buffer), so an
+    // abort can let them land before the CTA exits
+    uint32_t res_out = 0, res_par[2] = {0, 0};
+    auto issue_res = [&](uint32_t g, int col, int m0, int b) {
+      const int rb = g & 1;
+      mbar_arrive_expect_tx(res_full(rb), kEpiTile);
+      tma_load_3d(res_st + rb * kEpiTile, &tm_res, col, m0, b, res_full(rb));
+      res_out |= 1u << rb;
+      res_par[rb] = (g >> 1) & 1;
+    };
+    for (int tj = 0; tj < my_tiles && ok; ++tj) {
+      int b, mt, nt;
+      tile_coords(blockIdx.x + tj * gridDim.x, b, mt, nt);
+      const int m0 = mt * kBM;
+      const int rem_cols = p.Nc - nt * BN;
+      const int ngroups = rem_cols >= BN ? BN / 32 : (rem_cols + 31) / 32;
+      // residual blocks of the first two groups (later ones after each use)
+      if (p.res && et == 0) {
+        for (int g = 0; g < 2 && g < ngroups; ++g) issue_res(grp + g, nt * BN + g * 32, m0, b);
+      }
+      const int nch = L::kPromote ? (p.num_kb + L::kChunkKB - 1) / L::kChunkKB : 1;
+      for (int ch = 0; ch < nch; ++ch) {
+        const int cb = L::kPromote ? (cc & 1) : (tj & 1);
+        const uint32_t cpar = L::kPromote ? ((cc >> 1) & 1) : ((tj >> 1) & 1);
+        ok = named_bar_and(mbar_wait(acc_full(cb), cpar, abort_flag, p.status), kEpiThreads);
+        if (!ok) break;
+        tc_fence_after();
+        const bool last = ch == nch - 1;
+        const uint32_t ccol = L::kPromote ? BN * (1 + cb) : cb * BN;  // accumulator columns
+        if (L::kPromote && !last) {
+          // fold the chunk into the running total: each TMEM round trip carries
+          // 32 columns of the chunk and 32 of the total (loads issued before
+          // one wait), in 16-column pieces to bound live registers
+          const int ncols = ngroups * 32;
+          for (int c = 0; c < ncols; c += 32) {
+            uint32_t a0[16], a1[16], b0[16], b1[16];
+            tmem_ld_32x32b_x16(tmem_base + lane_addr + ccol + c, a0);
+            tmem_ld_32x32b_x16(tmem_base + lane_addr + ccol + c + 16, a1);
+            if (ch > 0) {
+              tmem_ld_32x32b_x16(tmem_base + lane_addr + c, b0);
+              tmem_ld_32x32b_x16(tmem_base + lane_addr + c + 16, b1);
+            }
+            tmem_ld_wait();
+            if (ch > 0) {
+#pragma unroll
+              for (int e = 0; e < 16; ++e) {
+                a0[e] = __float_as_uint(__uint_as_float(b0[e]) + __uint_as_float(a0[e]));
+                a1[e] = __float_as_uint(__uint_as_float(b1[e]) + __uint_as_float(a1[e]));
+              }
+            }
+            tmem_st_32x32b_x16(tmem_base + lane_addr + c, a0);
+            tmem_st_32x32b_x16(tmem_base + lane_addr + c + 16, a1);
+          }
+        }
+        for (int j = 0; j < ngroups && last; ++j) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tmem_base + lane_addr + ccol + j * 32, r);
+          if (L::kPromote && ch > 0) {
+            uint32_t t[32];
+            tmem_ld_32x32b_x32(tmem_base + lane_addr + j * 32, t);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              r[e] = __float_as_uint(__uint_as_float(t[e]) + __uint_as_float(r[e]));
+          } else {
+            tmem_ld_wait();
+          }
+          // ---- final values of this 32-column group
+          const int col0 = nt * BN + j * 32;
+          const int buf = grp & 1;
+          float v[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(r[e]);
+#pragma unroll
+          for (int q4 = 0; q4 < 8; ++q4) {
+            const int c = col0 + 4 * q4;
+            if (c < p.Nc) {
+              if (p.scale) {
+                const float4 sc = *reinterpret_cast<const float4*>(p.scale + c);
+                v[4 * q4] *= sc.x; v[4 * q4 + 1] *= sc.y; v[4 * q4 + 2] *= sc.z; v[4 * q4 + 3] *= sc.w;
+              }
+              if (p.shift) {
+                const float4 sh = *reinterpret_cast<const float4*>(p.shift + c);
+                v[4 * q4] += sh.x; v[4 * q4 + 1] += sh.y; v[4 * q4 + 2] += sh.z; v[4 * q4 + 3] += sh.w;
+              }
+            }
+          }
+          bool w = true;
+          if (p.res) {
+            w = mbar_wait(res_full(buf), (grp >> 1) & 1, abort_flag, p.status);
+            if (w && et == 0) res_out &= ~(1u << buf);
+#pragma unroll
+            for (int q4 = 0; q4 < 8; ++q4) {
+              const float4 rv = ld_shared_f4(res_st + buf * kEpiTile + swz128(et, q4));
+              v[4 * q4] += rv.x; v[4 * q4 + 1] += rv.y; v[4 * q4 + 2] += rv.z; v[4 * q4 + 3] += rv.w;
+            }
+          }
+          if (p.relu) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) v[e] = v[e] > 0.f ? v[e] : 0.f;
+          }
+          // the staging tile of two groups ago must have been read by its TMA store
+          if (et == 0) bulk_wait_group_read<1>();
+          ok = named_bar_and(w, kEpiThreads);
+          if (!ok) break;
+          const uint32_t ost = out_st + buf * kEpiTile;
+#pragma unroll
+          for (int q4 = 0; q4 < 8; ++q4)
+            sts_v4(ost + swz128(et, q4), v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
+          fence_proxy_async_smem();
+          named_bar_sync(kEpiThreads);
+          if (et == 0) {
+            tma_store_3d(&tm_y, col0, m0, b, ost);
+            bulk_commit_group();
+            if (p.res && j + 2 < ngroups) issue_res(grp + 2, col0 + 64, m0, b);  // freed buffer
+          }
+          ++grp;
+        }
+        if (!ok) break;
+        if (!last) tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(acc_empty(cb));
+        if (L::kPromote) ++cc;
+      }
+    }
+    if (et == 0) {
+      bulk_wait_group<0>();  // stores complete before the CTA exits
+      for (int rb = 0; rb < 2; ++rb)
+        if (res_out & (1u << rb)) {  // only after an abort
+          volatile int no_abort = 0;
+          mbar_wait(res_full(rb), res_par[rb], &no_abort, p.status);
+        }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, L::kTmemCols);
+  }
+}
+
+typedef CUresult (*EncodeTiledFn3)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn3 tiled_fn() {
+  static EncodeTiledFn3 fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      f = nullptr;
+    return reinterpret_cast<EncodeTiledFn3>(f);
+  }();
+  return fn;
+}
+
+// [batches][rows][cols] fp32 output / residual with row stride ld, batch stride
+// bstride (elements); 128 x 32 boxes, 128-byte swizzle.
+int encode_out_map(const float* base, int cols, int rows, int batches, int ld, long long bstride,
+                   CUtensorMap* map) {
+  EncodeTiledFn3 fn = tiled_fn();
+  if (!fn) return (int)CUDA_ERROR_NOT_FOUND;
+  const long long bs = batches > 1 ? bstride : (long long)rows * ld;
+  cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)batches};
+  cuuint64_t strides[2] = {(cuuint64_t)ld * 4, (cuuint64_t)bs * 4};
+  cuuint32_t box[3] = {32u, (cuuint32_t)kBM, 1u};
+  cuuint32_t es[3] = {1u, 1u, 1u};
+  return (int)fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box,
+                 es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+template <int PREC, int BN>
+int launch3_t(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap& lo,
+              const CUtensorMap& am, int num_sms, cudaStream_t st) {
+  using L = Layout<PREC, BN>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(igemm_tc3_kernel<PREC, BN>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
+    if (e != cudaSuccess) return (int)e;
+    attr_set = true;
+  }
+  CUtensorMap ym{}, rm{};
+  int er = encode_out_map(p.y, p.Nc, p.M, p.batches, p.ldy, p.y_bstride, &ym);
+  if (er) return (int)cudaErrorInvalidValue;
+  if (p.res) {
+    er = encode_out_map(p.res, p.Nc, p.M, p.batches, p.ldr, p.y_bstride, &rm);
+    if (er) return (int)cudaErrorInvalidValue;
+  }
+  const int total = p.m_tiles * p.n_tiles * p.batches;
+  const int grid = total < num_sms ? total : num_sms;
+  if (grid <= 0) return 0;
+  igemm_tc3_kernel<PREC, BN><<<grid, kThreads, L::kBytes, st>>>(p, hi, lo, am, ym, rm);
+  return (int)cudaGetLastError();
+}
+
+}  // namespace
+
+int igemm3_launch(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap& lo,
+                  const CUtensorMap& am, int precision, int bn, int num_sms, cudaStream_t st) {
+  if (precision == kPrec3xTF32 && bn == 64) return launch3_t<kPrec3xTF32, 64>(p, hi, lo, am, num_sms, st);
+  if (precision == kPrec3xTF32 && bn == 128) return launch3_t<kPrec3xTF32, 128>(p, hi, lo, am, num_sms, st);
+  if (precision == kPrecTF32 && bn == 64) return launch3_t<kPrecTF32, 64>(p, hi, lo, am, num_sms, st);
+  if (precision == kPrecTF32 && bn == 128) return launch3_t<kPrecTF32, 128>(p, hi, lo, am, num_sms, st);
+  return (int)cudaErrorInvalidValue;
+}
+
+}  // namespace ob2

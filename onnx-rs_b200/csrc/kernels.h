@@ -61,6 +61,13 @@ int igemm_pick_bn(const IgemmParams& p, int precision, int num_sms);
 int igemm_launch(const IgemmParams& p, const CUtensorMap& tm_hi, const CUtensorMap& tm_lo,
                  const CUtensorMap& tm_a, int precision, int bn, int num_sms, cudaStream_t stream);
 
+// The fp32-input kernel (3xTF32 / TF32, k-blocks of 16) behind igemm_launch.
+int igemm3_launch(const IgemmParams& p, const CUtensorMap& tm_hi, const CUtensorMap& tm_lo,
+                  const CUtensorMap& tm_a, int precision, int bn, int num_sms, cudaStream_t stream);
+
+// K elements per k-block of the kernel used for a precision (p.num_kb = Kpad / this).
+inline int igemm_block_k(int precision) { return precision == kPrecBF16 ? 32 : 16; }
+
 // ----------------------------------------------------------------- SIMT kernels
 // Direct convolution on CUDA cores (fp32 FFMA), any groups / channel count.
 // NHWC in, NHWC out, weights OIHW (original layout), same epilogue.
