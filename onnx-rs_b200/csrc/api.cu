@@ -190,7 +190,7 @@ int conv_plan_init(onnxb200_handle* h, const onnxb200_conv_desc* din, int cs_in,
   size_t off_hi = 0, off_lo = 0, off_scale = 0, off_shift = 0, off_w = 0;
   if (p->use_tc) {
     p->K = (int)(d.kh * d.kw * cs_in);
-    p->kpad = (p->K + 31) / 32 * 32;
+    p->kpad = igemm_kpad(p->K, p->prec);
     p->num_kb = p->kpad / igemm_block_k(p->prec);
     const size_t esz = p->prec == kPrecBF16 ? 2 : 4;
     const size_t wbytes = align_up((size_t)CO * p->kpad * esz);
@@ -751,7 +751,7 @@ int onnxb200_matmul(onnxb200_handle* h, const float* a, const int64_t* as, int r
     if (rc) return cuda_check(h, (cudaError_t)rc, "MatMul (CUDA cores)");
     return ONNXB200_OK;
   }
-  const int kpad = (int)((K + 31) / 32 * 32);
+  const int kpad = igemm_kpad(K, prec);
   const size_t esz = prec == kPrecBF16 ? 2 : 4;
   const size_t wb = align_up((size_t)nb_b * N * kpad * esz);
   const size_t need = wb * (prec == kPrec3xTF32 ? 2 : 1) + offs_bytes;
@@ -832,7 +832,7 @@ int onnxb200_gemm(onnxb200_handle* h, const float* a, const float* b, const floa
   const bool c_is_row = use_c && cm == 1;  // per-column (or scalar) addend
   const bool tc = prec != kPrecFP32 && k % 4 == 0 && n % 4 == 0 && k > 0 &&
                   (reinterpret_cast<uintptr_t>(a) & 15) == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0;
-  const int kpad = (int)((k + 31) / 32 * 32);
+  const int kpad = igemm_kpad(k, prec);
   const size_t esz = prec == kPrecBF16 ? 2 : 4;
   const size_t wb = tc ? align_up((size_t)n * kpad * esz) : 0;
   const size_t ab = (tc && trans_a) ? align_up((size_t)m * k * 4) : 0;

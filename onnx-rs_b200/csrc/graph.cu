@@ -713,7 +713,7 @@ extern "C" int onnxb200_graph_build(onnxb200_handle* h, const onnxb200_node* nod
           pg.c_id = an.in[0] == nd.out[0] ? an.in[1] : an.in[0];
         }
       }
-      gp.kpad = (gp.K + 31) / 32 * 32;
+      gp.kpad = igemm_kpad(gp.K, gp.prec);
       gp.y_bstride = (long long)gp.M * gp.N;
       s.type = kGemm;
       s.in = {a};

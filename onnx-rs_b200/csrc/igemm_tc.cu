@@ -530,7 +530,10 @@ int igemm_pick_bn(const IgemmParams& p, int precision, int num_sms) {
 
 int igemm_launch(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap& lo,
                  const CUtensorMap& am, int precision, int bn, int num_sms, cudaStream_t st) {
-  if (p.a_mode != kALoadGather && (precision == kPrecBF16 || p.Cs % 16 != 0))
+  if (p.a_mode != kALoadGather &&
+      (precision == kPrecBF16 ||
+       (p.a_mode == kALoadIm2colTaps ? ((p.Cs != 4 && p.Cs != 8) || p.K % p.Cs != 0)
+                                     : p.Cs % 16 != 0)))
     return (int)cudaErrorInvalidValue;
   // The kernel moves 16-byte vectors: refuse (instead of faulting on) any
   // pointer or stride that would make one of them misaligned.
@@ -551,8 +554,11 @@ int igemm_launch(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap&
 }
 
 int pick_a_mode(const IgemmParams& p, int precision) {
-  // TMA boxes carry 16 channels (64 bytes) of one filter tap per k-block
-  if (precision == kPrecBF16 || p.Cs % 16 != 0 || p.K % 16 != 0) return kALoadGather;
+  // TMA boxes carry 16 channels (64 bytes) of one filter tap per k-block, or
+  // 16 / Cs whole taps of a 4- or 8-channel tensor
+  const bool few_ch = (p.Cs == 4 || p.Cs == 8) && p.K % p.Cs == 0 && p.K > p.Cs;
+  if (precision == kPrecBF16 || (!few_ch && (p.Cs % 16 != 0 || p.K % 16 != 0)))
+    return kALoadGather;
   const bool single_tap = p.K == p.Cs;
   if (single_tap && p.sh == 1 && p.sw == 1 && p.ph == 0 && p.pw == 0 && p.OH == p.Hin &&
       p.OW == p.Win)
@@ -567,7 +573,7 @@ int pick_a_mode(const IgemmParams& p, int precision) {
   if (p.pw > 127 || p.ph > 127 || up_w < -128 || up_h < -128 || up_w > 127 || up_h > 127 ||
       (p.KW - 1) * p.dw > 255 || (kh - 1) * p.dh > 255 || p.sw > 8 || p.sh > 8)
     return kALoadGather;
-  return kALoadIm2col;
+  return few_ch ? kALoadIm2colTaps : kALoadIm2col;
 }
 
 namespace {
@@ -615,8 +621,12 @@ int encode_a_map(const IgemmParams& p, int n, CUtensorMap* map) {
   int lower[2] = {-p.pw, -p.ph};
   int upper[2] = {(p.OW - 1) * p.sw - p.pw - (p.Win - 1), (p.OH - 1) * p.sh - p.ph - (p.Hin - 1)};
   cuuint32_t es[4] = {1u, (cuuint32_t)p.sw, (cuuint32_t)p.sh, 1u};
-  return (int)fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, dims, strides, lower, upper, 16u,
-                 (cuuint32_t)kBM, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+  // taps mode: one box = all Cs channels (16 or 32 bytes) of 128 pixels for one
+  // tap, unswizzled; otherwise 16 channels in 64-byte swizzled rows
+  const bool taps = p.a_mode == kALoadIm2colTaps;
+  return (int)fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, dims, strides, lower, upper,
+                 taps ? (cuuint32_t)p.Cs : 16u, (cuuint32_t)kBM, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                 taps ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_64B,
                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
 

@@ -25,7 +25,7 @@
 //               TMEM, B from shared memory).
 // 3xTF32: a*b ~= a_hi*b_hi + a_hi*b_lo + a_lo*b_hi (Ootomo & Yokota, 2022).  The
 // tensor core adds into its fp32 accumulator with truncation, so each TMEM
-// accumulator sums only 4 k-blocks (24 MMAs) and the epilogue warps fold these
+// accumulator sums only 8 k-blocks (48 MMAs) and the epilogue warps fold these
 // chunks into a running total with round-to-nearest fp32 adds.
 //
 // Every wait is bounded (kWaitTimeoutNs); on expiry the kernel records
@@ -57,13 +57,18 @@ struct Layout {
   static constexpr int kStage = kARaw + (kSplit ? 2 : 1) * kBBytes;
   static constexpr int kEpiBytes = 4 * kEpiTile;  // out[2] + res[2]
   static constexpr int kS1raw = (kSmemBudget - kEpiBytes) / kStage;
-  static constexpr int kS1 = kS1raw > 8 ? 8 : kS1raw;
+  static constexpr int kS1cap = kS1raw > 8 ? 8 : kS1raw;
   static constexpr bool kPromote = kSplit;
   static constexpr int kChunkKB = kPromote ? 8 : (1 << 30);  // 48 MMAs per chunk
   static constexpr int kAccCols = kPromote ? 3 * BN : 2 * BN;
-  static constexpr int kAStageCols = kSplit ? 2 * kBK : kBK;
-  static constexpr int kS2raw = (512 - kAccCols) / kAStageCols;
-  static constexpr int kS2 = kS2raw > 4 ? 4 : kS2raw;
+  // TMEM A stage: the hi half only (3xTF32); the lo half (and TF32's rounded
+  // A) overwrites the raw A in shared memory and is read from there
+  static constexpr int kAStageCols = kSplit ? kBK : 0;
+  static constexpr int kS2raw = kSplit ? (512 - kAccCols) / kBK : 64;
+  // One ring: stage s holds raw A + B in shared memory and A hi/lo in TMEM, so a
+  // single barrier per stage tracks its release (converters + one MMA commit).
+  static constexpr int kS1 = kS1cap < kS2raw ? kS1cap : kS2raw;
+  static constexpr int kS2 = kS1;
   static_assert(kS2 >= 2, "TMEM too small for two A stages");
   static_assert(kS1 >= 3, "shared memory too small");
   static constexpr int kACol0 = kAccCols;
@@ -74,9 +79,9 @@ struct Layout {
   static constexpr int kOffB = kOffA + kS1 * kARaw;     // B hi stages
   static constexpr int kOffBlo = kOffB + kS1 * kBBytes;  // B lo stages
   static constexpr int kOffBar = kOffBlo + (kSplit ? kS1 * kBBytes : 0);
-  // s1_full[S1], s1_empty[S1], t_full[S2], t_empty[S2], acc_full[2], acc_empty[2],
-  // res_full[2], drain
-  static constexpr int kNumBars = 2 * kS1 + 2 * kS2 + 7;
+  // s1_full[S1], s1_empty[S1], t_full[S2], acc_full[2], acc_empty[2], res_full[2],
+  // drain
+  static constexpr int kNumBars = 2 * kS1 + kS2 + 7;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kBytes = kOffMisc + 16 + 1024;
 };
@@ -121,11 +126,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto s1_full = [&](int s) { return bar0 + 8u * s; };
   auto s1_empty = [&](int s) { return bar0 + 8u * (S1 + s); };
   auto t_full = [&](int a) { return bar0 + 8u * (2 * S1 + a); };
-  auto t_empty = [&](int a) { return bar0 + 8u * (2 * S1 + S2 + a); };
-  auto acc_full = [&](int b) { return bar0 + 8u * (2 * S1 + 2 * S2 + b); };
-  auto acc_empty = [&](int b) { return bar0 + 8u * (2 * S1 + 2 * S2 + 2 + b); };
-  auto res_full = [&](int b) { return bar0 + 8u * (2 * S1 + 2 * S2 + 4 + b); };
-  const uint32_t drain_bar = bar0 + 8u * (2 * S1 + 2 * S2 + 6);
+  auto acc_full = [&](int b) { return bar0 + 8u * (2 * S1 + S2 + b); };
+  auto acc_empty = [&](int b) { return bar0 + 8u * (2 * S1 + S2 + 2 + b); };
+  auto res_full = [&](int b) { return bar0 + 8u * (2 * S1 + S2 + 4 + b); };
+  const uint32_t drain_bar = bar0 + 8u * (2 * S1 + S2 + 6);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + L::kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + L::kOffMisc + 4);
 
@@ -137,12 +141,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       // gather mode: one cp.async arrival per loader thread; TMA modes: one
       // arrival (with the transaction bytes of A and B) from the issuing thread
       mbar_init(s1_full(s), p.a_mode == kALoadGather ? 128 : 1);
-      mbar_init(s1_empty(s), 128 + 1);  // converters + the MMA commit
+      mbar_init(s1_empty(s), 1);  // the MMA commit (the MMAs ran after the converters)
     }
-    for (int a = 0; a < S2; ++a) {
-      mbar_init(t_full(a), 128);
-      mbar_init(t_empty(a), 1);
-    }
+    for (int a = 0; a < S2; ++a) mbar_init(t_full(a), 128);
     for (int b = 0; b < 2; ++b) {
       mbar_init(acc_full(b), 1);
       mbar_init(acc_empty(b), kEpiThreads);
@@ -194,24 +195,31 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int kb = item - tj * p.num_kb;
           int b, mt, nt;
           tile_coords(blockIdx.x + tj * gridDim.x, b, mt, nt);
-          mbar_arrive_expect_tx(s1_full(s), L::kARaw + (L::kSplit ? 2 : 1) * L::kBBytes);
           const int k0 = kb * kBK;
+          // A bytes of this k-block: taps beyond K (the zero-weight padding of
+          // the last k-block) are not loaded; the converters zero them
+          const int a_taps = p.a_mode == kALoadIm2colTaps ? max(0, min(kBK / p.Cs, (p.K - k0) / p.Cs))
+                                                          : (k0 < p.K ? 1 : 0);
+          const uint32_t a_box = p.a_mode == kALoadIm2colTaps ? kBM * p.Cs * 4 : L::kARaw;
+          mbar_arrive_expect_tx(s1_full(s), a_taps * a_box + (L::kSplit ? 2 : 1) * L::kBBytes);
           const int tap = k0 / p.Cs;
           const int c0 = k0 - tap * p.Cs;
           const uint32_t dst = a_raw + s * L::kARaw;
           if (p.a_mode == kALoadTma2d) {
             const int row0 = (p.a_off ? (int)(p.a_off[b] / p.Cs) : 0) + mt * kBM;
-            tma_load_2d(dst, &tm_a, c0, row0, s1_full(s));
+            if (a_taps) tma_load_2d(dst, &tm_a, c0, row0, s1_full(s));
           } else {
             const int m0 = mt * kBM;
             const int n0 = m0 / OHW;
             const int rem = m0 - n0 * OHW;
             const int oh0 = rem / p.OW;
             const int ow0 = rem - oh0 * p.OW;
-            const int r = tap / p.KW;
-            const int q = tap - r * p.KW;
-            tma_load_im2col_4d(dst, &tm_a, c0, ow0 * p.sw - p.pw, oh0 * p.sh - p.ph, n0,
-                               (uint16_t)(q * p.dw), (uint16_t)(r * p.dh), s1_full(s));
+            for (int j = 0; j < a_taps; ++j) {
+              const int r = (tap + j) / p.KW;
+              const int q = tap + j - r * p.KW;
+              tma_load_im2col_4d(dst + j * a_box, &tm_a, c0, ow0 * p.sw - p.pw, oh0 * p.sh - p.ph, n0,
+                                 (uint16_t)(q * p.dw), (uint16_t)(r * p.dh), s1_full(s));
+            }
           }
           const int brow = nt * BN + (p.b_row ? p.b_row[b] : 0);
           tma_load_2d(b_hi + s * L::kBBytes, &tm_hi, k0, brow, s1_full(s));
@@ -289,36 +297,71 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp - kConvWarp0;  // TMEM lane quadrant
     const int row = q * 32 + lane;
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+    // where the 16-byte chunk c (k offsets 4c..4c+3) of this row sits in a stage:
+    // 64-byte swizzled rows, or (taps mode) one [128][Cs] box per filter tap
+    uint32_t coff[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+      coff[c] = p.a_mode == kALoadIm2colTaps
+                    ? (uint32_t)((4 * c / p.Cs) * kBM * p.Cs * 4 + row * p.Cs * 4 + (4 * c % p.Cs) * 4)
+                    : swz64(row, c);
+    const bool taps = p.a_mode == kALoadIm2colTaps;
+    int kb = 0;
     for (int item = 0; item < total_items; ++item) {
       const int s = item % S1;
       const int a = item % S2;
-      if (!mbar_wait(s1_full(s), (item / S1) & 1, abort_flag, p.status)) break;
+      bool ok = mbar_wait(s1_full(s), (item / S1) & 1, abort_flag, p.status);
       const uint32_t rbase = a_raw + s * L::kARaw;
       float v[16];
+      if (ok) {
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const float4 f = ld_shared_f4(rbase + swz64(row, c));
-        v[4 * c] = f.x;
-        v[4 * c + 1] = f.y;
-        v[4 * c + 2] = f.z;
-        v[4 * c + 3] = f.w;
+        for (int c = 0; c < 4; ++c) {
+          const float4 f = ld_shared_f4(rbase + coff[c]);
+          v[4 * c] = f.x;
+          v[4 * c + 1] = f.y;
+          v[4 * c + 2] = f.z;
+          v[4 * c + 3] = f.w;
+        }
       }
-      mbar_arrive(s1_empty(s));  // raw A of this stage consumed
+      // taps mode rewrites the stage in another layout: every converter has
+      // read its row before any writes (the AND keeps an abort uniform)
+      if (taps) ok = named_bar_and(ok, 128, 2);
+      if (!ok) break;
+      // k beyond K: padding of the last k-block (zero weights); never multiply
+      // whatever the stage held there
+      const int kvalid = p.K - kb * kBK;
+      if (kvalid < kBK) {
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          if (e >= kvalid) v[e] = 0.f;
+      }
+      if (++kb == p.num_kb) kb = 0;
       uint32_t hi[16];
 #pragma unroll
       for (int e = 0; e < 16; ++e) hi[e] = __float_as_uint(to_tf32(v[e]));
-      if (!mbar_wait(t_empty(a), ((item / S2) & 1) ^ 1, abort_flag, p.status)) break;
-      tc_fence_after();
-      const uint32_t acol = tmem_base + lane_addr + L::kACol0 + a * L::kAStageCols;
-      tmem_st_32x32b_x16(acol, hi);
       if constexpr (L::kSplit) {
-        uint32_t lo[16];
+        // lo = rna(v - hi) in place of the raw row (64-byte swizzled, the layout
+        // the MMA's shared-memory descriptor reads); hi to this stage's TMEM slot,
+        // which is free: the loader refilled the stage only after the MMAs of its
+        // previous use committed, and this thread has seen the refill land
 #pragma unroll
-        for (int e = 0; e < 16; ++e) lo[e] = __float_as_uint(to_tf32(v[e] - __uint_as_float(hi[e])));
-        tmem_st_32x32b_x16(acol + kBK, lo);
+        for (int c = 0; c < 4; ++c) {
+          float l[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) l[e] = to_tf32(v[4 * c + e] - __uint_as_float(hi[4 * c + e]));
+          st_shared_f4(rbase + swz64(row, c), l[0], l[1], l[2], l[3]);
+        }
+        tc_fence_after();
+        tmem_st_32x32b_x16(tmem_base + lane_addr + L::kACol0 + a * L::kAStageCols, hi);
+        tmem_st_wait();
+        tc_fence_before();
+      } else {
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          st_shared_f4(rbase + swz64(row, c), __uint_as_float(hi[4 * c]), __uint_as_float(hi[4 * c + 1]),
+                       __uint_as_float(hi[4 * c + 2]), __uint_as_float(hi[4 * c + 3]));
       }
-      tmem_st_wait();
-      tc_fence_before();
+      fence_proxy_async_smem();  // the generic-proxy stores, visible to the tensor core
       mbar_arrive(t_full(a));
     }
   } else if (warp == kMmaWarp) {
@@ -351,28 +394,31 @@ __global__ void __launch_bounds__(kThreads, 1)
             d_tmem = tmem_base + BN * (1 + cb);
           }
         }
-        if (!mbar_wait(t_full(a), (item / S2) & 1, abort_flag, p.status) ||
-            !mbar_wait(s1_full(s), (item / S1) & 1, abort_flag, p.status)) {
+        // one wait per stage: the converters arrive on t_full only after they
+        // saw the stage's TMA (A and B) complete on s1_full
+        if (!mbar_wait(t_full(a), (item / S2) & 1, abort_flag, p.status)) {
           failed = true;
           break;
         }
         tc_fence_after();
         if (lane == 0) {
           const uint32_t ahi = tmem_base + L::kACol0 + a * L::kAStageCols;
+          const uint64_t da = smem_desc_sw64(a_raw + s * L::kARaw);  // A lo (TF32: A)
           const uint64_t dbh = smem_desc_sw64(b_hi + s * L::kBBytes);
           uint64_t dbl = 0;
           if constexpr (L::kSplit) dbl = smem_desc_sw64(b_lo + s * L::kBBytes);
 #pragma unroll
           for (int kk = 0; kk < kBK / 8; ++kk) {
             const uint32_t acc = ((L::kPromote ? kin : kb) | kk) ? 1u : 0u;
-            tc_mma_tf32_ts(d_tmem, ahi + kk * 8, dbh + (uint64_t)(kk * 2), idesc, acc);
             if constexpr (L::kSplit) {
+              tc_mma_tf32_ts(d_tmem, ahi + kk * 8, dbh + (uint64_t)(kk * 2), idesc, acc);
               tc_mma_tf32_ts(d_tmem, ahi + kk * 8, dbl + (uint64_t)(kk * 2), idesc, 1u);
-              tc_mma_tf32_ts(d_tmem, ahi + kBK + kk * 8, dbh + (uint64_t)(kk * 2), idesc, 1u);
+              tc_mma<0>(d_tmem, da + (uint64_t)(kk * 2), dbh + (uint64_t)(kk * 2), idesc, 1u);
+            } else {
+              tc_mma<0>(d_tmem, da + (uint64_t)(kk * 2), dbh + (uint64_t)(kk * 2), idesc, acc);
             }
           }
-          tc_commit(s1_empty(s));
-          tc_commit(t_empty(a));
+          tc_commit(s1_empty(s));  // frees the stage: shared memory and TMEM A slot
           issued = true;
         }
         if constexpr (L::kPromote) {

@@ -39,11 +39,13 @@ struct IgemmParams {
   int m_tiles, n_tiles;
   // How A tiles reach shared memory: kALoadGather = per-thread 16-byte copies
   // (any shape), kALoadTma2d = TMA tile of the [rows][Cs] matrix (1x1 stride-1
-  // convs, GEMMs), kALoadIm2col = TMA im2col over the NHWC tensor (Cs % 32 == 0).
+  // convs, GEMMs), kALoadIm2col = TMA im2col over the NHWC tensor, 16 channels
+  // of one filter tap per k-block (Cs % 16 == 0), kALoadIm2colTaps = TMA im2col
+  // of 16 / Cs whole filter taps per k-block (Cs = 4 or 8, e.g. an RGB stem).
   int a_mode;
 };
 
-enum ALoadMode { kALoadGather = 0, kALoadTma2d = 1, kALoadIm2col = 2 };
+enum ALoadMode { kALoadGather = 0, kALoadTma2d = 1, kALoadIm2col = 2, kALoadIm2colTaps = 3 };
 
 // Encodes the TMA map of the A operand for p.a_mode (x, shape and conv geometry
 // from p); returns a CUresult (0 = success).  Not needed for kALoadGather.
@@ -67,6 +69,11 @@ int igemm3_launch(const IgemmParams& p, const CUtensorMap& tm_hi, const CUtensor
 
 // K elements per k-block of the kernel used for a precision (p.num_kb = Kpad / this).
 inline int igemm_block_k(int precision) { return precision == kPrecBF16 ? 32 : 16; }
+// Padded K (row length of the packed weights): a whole number of k-blocks.
+inline int igemm_kpad(long long K, int precision) {
+  const int bk = igemm_block_k(precision);
+  return (int)((K + bk - 1) / bk * bk);
+}
 
 // ----------------------------------------------------------------- SIMT kernels
 // Direct convolution on CUDA cores (fp32 FFMA), any groups / channel count.

@@ -159,16 +159,17 @@ __device__ __forceinline__ void bulk_wait_group() {
   asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// Named barrier 1 over `nthreads` threads; the AND of `v` over them is returned.
-__device__ __forceinline__ bool named_bar_and(bool v, int nthreads) {
+// Named barrier `id` (default 1) over `nthreads` threads; the AND of `v` over
+// them is returned.
+__device__ __forceinline__ bool named_bar_and(bool v, int nthreads, int id = 1) {
   uint32_t r;
   asm volatile(
       "{\n\t.reg .pred p, q;\n\t"
       "setp.ne.u32 q, %1, 0;\n\t"
-      "barrier.cta.red.and.pred p, 1, %2, q;\n\t"
+      "barrier.cta.red.and.pred p, %3, %2, q;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(r)
-      : "r"((uint32_t)v), "r"(nthreads)
+      : "r"((uint32_t)v), "r"(nthreads), "r"(id)
       : "memory");
   return r != 0;
 }
@@ -265,6 +266,11 @@ __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
+__device__ __forceinline__ void st_shared_f4(uint32_t addr, float x, float y, float z, float w) {
+  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(x), "f"(y), "f"(z),
+               "f"(w)
+               : "memory");
+}
 __device__ __forceinline__ float4 ld_shared_f4(uint32_t addr) {
   float4 v;
   asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"

@@ -2,6 +2,8 @@
 // fallback batched GEMM, weight packing for the tcgen05 kernel, layout
 // repacks, MaxPool, GlobalAveragePool and elementwise ops.  All memory-bound
 // kernels move 16-byte vectors along the channel (innermost NHWC) axis.
+#include <algorithm>
+#include <cstdint>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -206,10 +208,39 @@ __global__ void nchw_to_nhwc_kernel(const float* __restrict__ x, int C, int HW, 
   }
 }
 
+// Few channels (an RGB image padded to 4 or 8): one thread per pixel, reading
+// each plane coalesced along the pixels and writing its padded channel row as
+// 16-byte vectors.
+template <int CP4>
+__global__ void nchw_to_nhwc_small_kernel(const float* __restrict__ x, long long npix, int C,
+                                          int HW, float4* __restrict__ y) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < npix;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long n = i / HW;
+    const int hw = (int)(i - n * HW);
+    const float* px = x + n * C * HW + hw;
+    float v[4 * CP4];
+#pragma unroll
+    for (int c = 0; c < 4 * CP4; ++c) v[c] = c < C ? __ldg(px + (long long)c * HW) : 0.f;
+#pragma unroll
+    for (int j = 0; j < CP4; ++j)
+      y[i * CP4 + j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  }
+}
+
 int nchw_to_nhwc_launch(const float* x, int N, int C, int H, int W, int Cp, float* y,
                         cudaStream_t st) {
   const int HW = H * W;
   if ((long long)N * HW * Cp == 0) return 0;
+  if ((Cp == 4 || Cp == 8) && C <= Cp && ((uintptr_t)y & 15) == 0) {
+    const long long npix = (long long)N * HW;
+    const int blocks = (int)std::min<long long>((npix + 255) / 256, 148LL * 16);
+    if (Cp == 4)
+      nchw_to_nhwc_small_kernel<1><<<blocks, 256, 0, st>>>(x, npix, C, HW, (float4*)y);
+    else
+      nchw_to_nhwc_small_kernel<2><<<blocks, 256, 0, st>>>(x, npix, C, HW, (float4*)y);
+    return (int)cudaGetLastError();
+  }
   dim3 grid((HW + 31) / 32, (Cp + 31) / 32, N);
   nchw_to_nhwc_kernel<<<grid, dim3(32, 8), 0, st>>>(x, C, HW, Cp, y);
   return (int)cudaGetLastError();

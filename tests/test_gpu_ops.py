@@ -51,6 +51,8 @@ SMALL = [
     ("c8_co20", (1, 8, 9, 9), 20, 3, 1, 1, 1, 1),
     ("grouped", (2, 32, 10, 10), 32, 3, 1, 1, 1, 8),
     ("c5_odd_channels", (2, 5, 9, 9), 12, 3, 1, 1, 1, 1),
+    ("c3_dil2_s2", (2, 3, 17, 19), 16, 3, 2, 2, 2, 1),
+    ("c6_5x5_s2", (1, 6, 21, 18), 24, 5, 2, 2, 1, 1),
 ]
 
 
