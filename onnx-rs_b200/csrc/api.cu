@@ -78,12 +78,13 @@ int encode_weight_map(onnxb200_handle* h, CUtensorMap* map, const void* base, in
   const int esz = prec == kPrecBF16 ? 2 : 4;
   cuuint64_t dims[2] = {(cuuint64_t)kpad, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)kpad * esz};
-  // one k-block of a weight row = 64 bytes (16 fp32 or 32 bf16), 64-byte swizzle
-  cuuint32_t box[2] = {(cuuint32_t)(64 / esz), (cuuint32_t)bn};
+  // one k-block of a weight row = 32 elements: 128 bytes of fp32 (128-byte
+  // swizzle) or 64 bytes of bf16 (64-byte swizzle)
+  cuuint32_t box[2] = {32u, (cuuint32_t)bn};
   cuuint32_t estr[2] = {1u, 1u};
   CUresult r = fn(map, prec == kPrecBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
-                  2, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                  2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  prec == kPrecBF16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return set_error(h, ONNXB200_ERR_EXECUTION, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));

@@ -532,8 +532,9 @@ int igemm_launch(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap&
                  const CUtensorMap& am, int precision, int bn, int num_sms, cudaStream_t st) {
   if (p.a_mode != kALoadGather &&
       (precision == kPrecBF16 ||
-       (p.a_mode == kALoadIm2colTaps ? ((p.Cs != 4 && p.Cs != 8) || p.K % p.Cs != 0)
-                                     : p.Cs % 16 != 0)))
+       (p.a_mode == kALoadIm2colTaps ? ((p.Cs != 4 && p.Cs != 8 && p.Cs != 16) || p.K % p.Cs != 0)
+        : p.a_mode == kALoadIm2col   ? p.Cs % 32 != 0
+                                     : p.Cs < 32)))
     return (int)cudaErrorInvalidValue;
   // The kernel moves 16-byte vectors: refuse (instead of faulting on) any
   // pointer or stride that would make one of them misaligned.
@@ -554,15 +555,16 @@ int igemm_launch(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap&
 }
 
 int pick_a_mode(const IgemmParams& p, int precision) {
-  // TMA boxes carry 16 channels (64 bytes) of one filter tap per k-block, or
-  // 16 / Cs whole taps of a 4- or 8-channel tensor
-  const bool few_ch = (p.Cs == 4 || p.Cs == 8) && p.K % p.Cs == 0 && p.K > p.Cs;
-  if (precision == kPrecBF16 || (!few_ch && (p.Cs % 16 != 0 || p.K % 16 != 0)))
-    return kALoadGather;
+  // A k-block is 32 fp32 (one 128-byte TMA row per pixel): 32 channels of one
+  // filter tap, or 32 / Cs whole taps of a 4-, 8- or 16-channel tensor
+  if (precision == kPrecBF16) return kALoadGather;
   const bool single_tap = p.K == p.Cs;
   if (single_tap && p.sh == 1 && p.sw == 1 && p.ph == 0 && p.pw == 0 && p.OH == p.Hin &&
-      p.OW == p.Win)
-    return kALoadTma2d;  // rows of A are rows of the [pixels][channels] matrix
+      p.OW == p.Win)  // rows of A are rows of the [pixels][channels] matrix; the
+                      // box of the last k-block may run past Cs (zero fill)
+    return p.Cs >= 32 ? kALoadTma2d : kALoadGather;
+  const bool few_ch = (p.Cs == 4 || p.Cs == 8 || p.Cs == 16) && p.K % p.Cs == 0;
+  if (!few_ch && p.Cs % 32 != 0) return kALoadGather;
   // im2col maps: 4-D corners are 8-bit signed, the filter-tap offsets 8-bit
   // unsigned (small convolutions always fit); one image batch per launch.
   if (p.batches != 1 || p.a_off) return kALoadGather;
@@ -604,10 +606,10 @@ int encode_a_map(const IgemmParams& p, int n, CUtensorMap* map) {
     // n = number of rows of the [rows][Cs] matrix (pixels of the batch, or all A rows)
     cuuint64_t dims[2] = {(cuuint64_t)p.Cs, (cuuint64_t)n};
     cuuint64_t strides[1] = {(cuuint64_t)p.Cs * 4};
-    cuuint32_t box[2] = {16u, (cuuint32_t)kBM};
+    cuuint32_t box[2] = {32u, (cuuint32_t)kBM};
     cuuint32_t es[2] = {1u, 1u};
     return (int)fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, es,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   }
   static EncodeIm2colFn fn = reinterpret_cast<EncodeIm2colFn>(driver_fn("cuTensorMapEncodeIm2col"));
@@ -621,12 +623,12 @@ int encode_a_map(const IgemmParams& p, int n, CUtensorMap* map) {
   int lower[2] = {-p.pw, -p.ph};
   int upper[2] = {(p.OW - 1) * p.sw - p.pw - (p.Win - 1), (p.OH - 1) * p.sh - p.ph - (p.Hin - 1)};
   cuuint32_t es[4] = {1u, (cuuint32_t)p.sw, (cuuint32_t)p.sh, 1u};
-  // taps mode: one box = all Cs channels (16 or 32 bytes) of 128 pixels for one
-  // tap, unswizzled; otherwise 16 channels in 64-byte swizzled rows
+  // taps mode: one box = all Cs channels (16 to 64 bytes) of 128 pixels for one
+  // tap, unswizzled; otherwise 32 channels in 128-byte swizzled rows
   const bool taps = p.a_mode == kALoadIm2colTaps;
   return (int)fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, dims, strides, lower, upper,
-                 taps ? (cuuint32_t)p.Cs : 16u, (cuuint32_t)kBM, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                 taps ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_64B,
+                 taps ? (cuuint32_t)p.Cs : 32u, (cuuint32_t)kBM, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                 taps ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B,
                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
 

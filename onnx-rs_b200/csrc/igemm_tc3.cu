@@ -7,7 +7,7 @@
 // compute_gemm (src/ops/math/gemm.rs:172-291).
 //
 // Persistent, warp-specialised, one 416-thread CTA per SM.  Tile 128 x BN
-// (BN = 64 or 128), k-blocks of 16 fp32 (64-byte swizzled rows).
+// (BN = 64 or 128), k-blocks of 32 fp32 (128-byte swizzled rows).
 //   warps 0-3   epilogue: TMEM -> registers, per-channel scale/shift (bias, folded
 //               BatchNormalization), residual, Relu; each 128 x 32 block is staged in
 //               shared memory and written with one TMA store (the hardware clips rows
@@ -25,7 +25,7 @@
 //               TMEM, B from shared memory).
 // 3xTF32: a*b ~= a_hi*b_hi + a_hi*b_lo + a_lo*b_hi (Ootomo & Yokota, 2022).  The
 // tensor core adds into its fp32 accumulator with truncation, so each TMEM
-// accumulator sums only 8 k-blocks (48 MMAs) and the epilogue warps fold these
+// accumulator sums only 4 k-blocks (48 MMAs) and the epilogue warps fold these
 // chunks into a running total with round-to-nearest fp32 adds.
 //
 // Every wait is bounded (kWaitTimeoutNs); on expiry the kernel records
@@ -42,7 +42,8 @@ namespace ob2 {
 namespace {
 
 constexpr int kBM = 128;
-constexpr int kBK = 16;  // fp32 K elements per k-block
+constexpr int kBK = 32;  // fp32 K elements per k-block: 128-byte rows (TMA moves
+                         // about one row per two cycles, so wider rows are faster)
 constexpr int kEpiThreads = 128;
 constexpr int kLoadWarp0 = 4, kConvWarp0 = 8, kMmaWarp = 12;
 constexpr int kThreads = 13 * 32;
@@ -52,14 +53,14 @@ constexpr int kEpiTile = kBM * 32 * 4;  // one 128 x 32 fp32 staging tile (16 KB
 template <int PREC, int BN>
 struct Layout {
   static constexpr bool kSplit = (PREC == kPrec3xTF32);
-  static constexpr int kARaw = kBM * kBK * 4;   // 8 KB
+  static constexpr int kARaw = kBM * kBK * 4;   // 16 KB
   static constexpr int kBBytes = BN * kBK * 4;  // one B operand (hi or lo)
   static constexpr int kStage = kARaw + (kSplit ? 2 : 1) * kBBytes;
   static constexpr int kEpiBytes = 4 * kEpiTile;  // out[2] + res[2]
   static constexpr int kS1raw = (kSmemBudget - kEpiBytes) / kStage;
   static constexpr int kS1cap = kS1raw > 8 ? 8 : kS1raw;
   static constexpr bool kPromote = kSplit;
-  static constexpr int kChunkKB = kPromote ? 8 : (1 << 30);  // 48 MMAs per chunk
+  static constexpr int kChunkKB = kPromote ? 4 : (1 << 30);  // 48 MMAs per chunk
   static constexpr int kAccCols = kPromote ? 3 * BN : 2 * BN;
   // TMEM A stage: the hi half only (3xTF32); the lo half (and TF32's rounded
   // A) overwrites the raw A in shared memory and is read from there
@@ -86,25 +87,12 @@ struct Layout {
   static constexpr int kBytes = kOffMisc + 16 + 1024;
 };
 
-// 64-byte-swizzle layout of a [rows][16 fp32] tile: 16-byte chunk c of row r.
-__device__ __forceinline__ uint32_t swz64(int r, int c) { return r * 64 + ((c ^ ((r >> 1) & 3)) << 4); }
 // 128-byte-swizzle layout of a [rows][32 fp32] tile.
 __device__ __forceinline__ uint32_t swz128(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
 
 __device__ __forceinline__ void sts_v4(uint32_t addr, float a, float b, float c, float d) {
   asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
                : "memory");
-}
-
-// K-major operand, 64-byte swizzle: 8-row atoms of 512 bytes.
-__device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t saddr) {
-  uint64_t d = 0;
-  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
-  d |= static_cast<uint64_t>(1u) << 16;
-  d |= static_cast<uint64_t>(512u >> 4) << 32;
-  d |= static_cast<uint64_t>(1u) << 46;
-  d |= static_cast<uint64_t>(4u) << 61;  // SWIZZLE_64B
-  return d;
 }
 
 template <int PREC, int BN>
@@ -184,11 +172,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ loaders
     const int lt = threadIdx.x - kLoadWarp0 * 32;
     if (p.a_mode != kALoadGather) {
-      // lane 0 of each of the 4 loader warps issues every 4th stage: the TMA
-      // issue path of one thread is slower than the MMAs of one stage
-      if (lane == 0) {
+      // lane 0 of each of NL loader warps issues every NL-th stage: the TMA issue
+      // path of one thread is slower than the MMAs of one stage.  NL <= S1: a
+      // lane's wait for stage use u must never start before use u - 2 has
+      // completed, or the parity wait would pass a phase early (the lane last
+      // waited for the stage of its previous item, NL items back).
+      constexpr int NL = S1 < 4 ? S1 : 4;
+      if (lane == 0 && warp - kLoadWarp0 < NL) {
         const int OHW = p.OH * p.OW;
-        for (int item = warp - kLoadWarp0; item < total_items; item += 4) {
+        for (int item = warp - kLoadWarp0; item < total_items; item += NL) {
           const int s = item % S1;
           if (!mbar_wait(s1_empty(s), ((item / S1) & 1) ^ 1, abort_flag, p.status)) break;
           const int tj = item / p.num_kb;
@@ -227,10 +219,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     } else {
-      // thread -> (16-byte chunk c of 4 per row, rows rslot + 32 i)
-      const int chunk = lt & 3;
-      const int rslot = lt >> 2;
-      int pix[4], ih0[4], iw0[4];
+      // thread -> (16-byte chunk c of 8 per row, rows rslot + 16 i)
+      const int chunk = lt & 7;
+      const int rslot = lt >> 3;
+      int pix[8], ih0[8], iw0[8];
       const float* xb = p.x;
       int cur_tile = -1;
       const int OHW = p.OH * p.OW;
@@ -245,8 +237,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           cur_tile = tj;
           xb = p.x + (p.a_off ? p.a_off[b] : 0ll);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int m = mt * kBM + rslot + 32 * i;
+          for (int i = 0; i < 8; ++i) {
+            const int m = mt * kBM + rslot + 16 * i;
             if (m < p.M) {
               const int n = m / OHW;
               const int rem = m - n * OHW;
@@ -280,13 +272,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const uint32_t stage = a_raw + s * L::kARaw;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int row = rslot + 32 * i;
+        for (int i = 0; i < 8; ++i) {
+          const int row = rslot + 16 * i;
           const int ih = ih0[i] + dy, iw = iw0[i] + dx;
           const bool ok = kval && (unsigned)ih < (unsigned)p.Hin && (unsigned)iw < (unsigned)p.Win;
           const float* src =
               ok ? xb + ((long long)pix[i] + (long long)ih * p.Win + iw) * p.Cs + ci : p.x;
-          cp_async_16(stage + swz64(row, chunk), src, ok ? 16u : 0u);
+          cp_async_16(stage + swz128(row, chunk), src, ok ? 16u : 0u);
         }
         cp_async_arrive_noinc(s1_full(s));
       }
@@ -298,13 +290,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = q * 32 + lane;
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
     // where the 16-byte chunk c (k offsets 4c..4c+3) of this row sits in a stage:
-    // 64-byte swizzled rows, or (taps mode) one [128][Cs] box per filter tap
-    uint32_t coff[4];
+    // 128-byte swizzled rows, or (taps mode) one [128][Cs] box per filter tap
+    uint32_t coff[kBK / 4];
 #pragma unroll
-    for (int c = 0; c < 4; ++c)
+    for (int c = 0; c < kBK / 4; ++c)
       coff[c] = p.a_mode == kALoadIm2colTaps
                     ? (uint32_t)((4 * c / p.Cs) * kBM * p.Cs * 4 + row * p.Cs * 4 + (4 * c % p.Cs) * 4)
-                    : swz64(row, c);
+                    : swz128(row, c);
     const bool taps = p.a_mode == kALoadIm2colTaps;
     int kb = 0;
     for (int item = 0; item < total_items; ++item) {
@@ -312,10 +304,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int a = item % S2;
       bool ok = mbar_wait(s1_full(s), (item / S1) & 1, abort_flag, p.status);
       const uint32_t rbase = a_raw + s * L::kARaw;
-      float v[16];
+      float v[kBK];
       if (ok) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < kBK / 4; ++c) {
           const float4 f = ld_shared_f4(rbase + coff[c]);
           v[4 * c] = f.x;
           v[4 * c + 1] = f.y;
@@ -332,33 +324,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int kvalid = p.K - kb * kBK;
       if (kvalid < kBK) {
 #pragma unroll
-        for (int e = 0; e < 16; ++e)
+        for (int e = 0; e < kBK; ++e)
           if (e >= kvalid) v[e] = 0.f;
       }
       if (++kb == p.num_kb) kb = 0;
-      uint32_t hi[16];
+      uint32_t hi[kBK];
 #pragma unroll
-      for (int e = 0; e < 16; ++e) hi[e] = __float_as_uint(to_tf32(v[e]));
+      for (int e = 0; e < kBK; ++e) hi[e] = __float_as_uint(to_tf32(v[e]));
       if constexpr (L::kSplit) {
-        // lo = rna(v - hi) in place of the raw row (64-byte swizzled, the layout
+        // lo = rna(v - hi) in place of the raw row (128-byte swizzled, the layout
         // the MMA's shared-memory descriptor reads); hi to this stage's TMEM slot,
         // which is free: the loader refilled the stage only after the MMAs of its
         // previous use committed, and this thread has seen the refill land
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < kBK / 4; ++c) {
           float l[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) l[e] = to_tf32(v[4 * c + e] - __uint_as_float(hi[4 * c + e]));
-          st_shared_f4(rbase + swz64(row, c), l[0], l[1], l[2], l[3]);
+          st_shared_f4(rbase + swz128(row, c), l[0], l[1], l[2], l[3]);
         }
         tc_fence_after();
-        tmem_st_32x32b_x16(tmem_base + lane_addr + L::kACol0 + a * L::kAStageCols, hi);
+        tmem_st_32x32b_x32(tmem_base + lane_addr + L::kACol0 + a * L::kAStageCols, hi);
         tmem_st_wait();
         tc_fence_before();
       } else {
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-          st_shared_f4(rbase + swz64(row, c), __uint_as_float(hi[4 * c]), __uint_as_float(hi[4 * c + 1]),
+        for (int c = 0; c < kBK / 4; ++c)
+          st_shared_f4(rbase + swz128(row, c), __uint_as_float(hi[4 * c]), __uint_as_float(hi[4 * c + 1]),
                        __uint_as_float(hi[4 * c + 2]), __uint_as_float(hi[4 * c + 3]));
       }
       fence_proxy_async_smem();  // the generic-proxy stores, visible to the tensor core
@@ -403,10 +395,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         if (lane == 0) {
           const uint32_t ahi = tmem_base + L::kACol0 + a * L::kAStageCols;
-          const uint64_t da = smem_desc_sw64(a_raw + s * L::kARaw);  // A lo (TF32: A)
-          const uint64_t dbh = smem_desc_sw64(b_hi + s * L::kBBytes);
+          const uint64_t da = smem_desc_sw128(a_raw + s * L::kARaw);  // A lo (TF32: A)
+          const uint64_t dbh = smem_desc_sw128(b_hi + s * L::kBBytes);
           uint64_t dbl = 0;
-          if constexpr (L::kSplit) dbl = smem_desc_sw64(b_lo + s * L::kBBytes);
+          if constexpr (L::kSplit) dbl = smem_desc_sw128(b_lo + s * L::kBBytes);
 #pragma unroll
           for (int kk = 0; kk < kBK / 8; ++kk) {
             const uint32_t acc = ((L::kPromote ? kin : kb) | kk) ? 1u : 0u;

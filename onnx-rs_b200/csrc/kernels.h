@@ -39,9 +39,10 @@ struct IgemmParams {
   int m_tiles, n_tiles;
   // How A tiles reach shared memory: kALoadGather = per-thread 16-byte copies
   // (any shape), kALoadTma2d = TMA tile of the [rows][Cs] matrix (1x1 stride-1
-  // convs, GEMMs), kALoadIm2col = TMA im2col over the NHWC tensor, 16 channels
-  // of one filter tap per k-block (Cs % 16 == 0), kALoadIm2colTaps = TMA im2col
-  // of 16 / Cs whole filter taps per k-block (Cs = 4 or 8, e.g. an RGB stem).
+  // convs, GEMMs; Cs >= 32), kALoadIm2col = TMA im2col over the NHWC tensor, 32
+  // channels of one filter tap per k-block (Cs % 32 == 0), kALoadIm2colTaps =
+  // TMA im2col of 32 / Cs whole filter taps per k-block (Cs = 4, 8 or 16, e.g.
+  // an RGB stem).
   int a_mode;
 };
 
@@ -68,7 +69,7 @@ int igemm3_launch(const IgemmParams& p, const CUtensorMap& tm_hi, const CUtensor
                   const CUtensorMap& tm_a, int precision, int bn, int num_sms, cudaStream_t stream);
 
 // K elements per k-block of the kernel used for a precision (p.num_kb = Kpad / this).
-inline int igemm_block_k(int precision) { return precision == kPrecBF16 ? 32 : 16; }
+inline int igemm_block_k(int) { return 32; }
 // Padded K (row length of the packed weights): a whole number of k-blocks.
 inline int igemm_kpad(long long K, int precision) {
   const int bk = igemm_block_k(precision);
