@@ -9,7 +9,7 @@
 // Persistent, warp-specialised, one 416-thread CTA per SM.  Tile 128 x BN
 // (BN = 64 or 128), k-blocks of 32 fp32 (128-byte swizzled rows).
 //   warps 0-3   epilogue: TMEM -> registers, per-channel scale/shift (bias, folded
-//               BatchNormalization), residual, Relu; each 128 x 32 block is staged in
+//               BatchNormalization), residual, Relu; each 128 x 16 block is staged in
 //               shared memory and written with one TMA store (the hardware clips rows
 //               >= M and columns >= N); residual blocks arrive by TMA load.
 //   warps 4-7   A loaders.  TMA modes: one thread issues, per k-block, the A tile
@@ -47,11 +47,15 @@ constexpr int kBK = 32;  // fp32 K elements per k-block: 128-byte rows (TMA move
 constexpr int kEpiThreads = 128;
 constexpr int kLoadWarp0 = 4, kConvWarp0 = 8, kMmaWarp = 12;
 constexpr int kThreads = 13 * 32;
-constexpr int kSmemBudget = 220 * 1024;
-constexpr int kEpiTile = kBM * 32 * 4;  // one 128 x 32 fp32 staging tile (16 KB)
+constexpr int kSmemBudget = 224 * 1024;
+// The epilogue works in groups of EG output columns (a 128 x EG fp32 staging
+// tile per TMA store or residual load): EG = 32 (128-byte rows) stores fastest;
+// EG = 16 halves the staging memory so that 3xTF32 with BN = 128 fits four 48 KB
+// operand stages, which pays when the tile's K loop is long.
 
-template <int PREC, int BN>
+template <int PREC, int BN, int EG>
 struct Layout {
+  static constexpr int kEpiTile = kBM * EG * 4;
   static constexpr bool kSplit = (PREC == kPrec3xTF32);
   static constexpr int kARaw = kBM * kBK * 4;   // 16 KB
   static constexpr int kBBytes = BN * kBK * 4;  // one B operand (hi or lo)
@@ -85,22 +89,34 @@ struct Layout {
   static constexpr int kNumBars = 2 * kS1 + kS2 + 7;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kBytes = kOffMisc + 16 + 1024;
+  static_assert(kBytes <= 227 * 1024, "exceeds the 227 KB of shared memory per block");
 };
 
+// 64-byte-swizzle layout of a [rows][16 fp32] tile: 16-byte chunk c of row r.
+__device__ __forceinline__ uint32_t swz64(int r, int c) { return r * 64 + ((c ^ ((r >> 1) & 3)) << 4); }
 // 128-byte-swizzle layout of a [rows][32 fp32] tile.
 __device__ __forceinline__ uint32_t swz128(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
+// Staging tile of the epilogue: rows of EG fp32, swizzled like its TMA box.
+template <int EG>
+__device__ __forceinline__ uint32_t swz_eg(int r, int c) {
+  return EG == 32 ? swz128(r, c) : swz64(r, c);
+}
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[16]) { tmem_ld_32x32b_x16(taddr, r); }
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[32]) { tmem_ld_32x32b_x32(taddr, r); }
 
 __device__ __forceinline__ void sts_v4(uint32_t addr, float a, float b, float c, float d) {
   asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
                : "memory");
 }
 
-template <int PREC, int BN>
+template <int PREC, int BN, int EG>
 __global__ void __launch_bounds__(kThreads, 1)
     igemm_tc3_kernel(const __grid_constant__ IgemmParams p, const __grid_constant__ CUtensorMap tm_hi,
                      const __grid_constant__ CUtensorMap tm_lo, const __grid_constant__ CUtensorMap tm_a,
                      const __grid_constant__ CUtensorMap tm_y, const __grid_constant__ CUtensorMap tm_res) {
-  using L = Layout<PREC, BN>;
+  using L = Layout<PREC, BN, EG>;
+  constexpr int kEG = EG;
+  constexpr int kEpiTile = L::kEpiTile;
   constexpr int S1 = L::kS1;
   constexpr int S2 = L::kS2;
 
@@ -439,7 +455,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int et = threadIdx.x;  // 0..127 = tile row
     const uint32_t lane_addr = (uint32_t)(warp * 32) << 16;
     uint32_t cc = 0;   // accumulator chunks consumed
-    uint32_t grp = 0;  // 32-column output groups produced (staging buffer = grp & 1)
+    uint32_t grp = 0;  // kEG-column output groups produced (staging buffer = grp & 1)
     bool ok = true;
     // thread 0: residual loads issued but not yet waited for (per buffer), so an
     // abort can let them land before the CTA exits
@@ -456,10 +472,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       tile_coords(blockIdx.x + tj * gridDim.x, b, mt, nt);
       const int m0 = mt * kBM;
       const int rem_cols = p.Nc - nt * BN;
-      const int ngroups = rem_cols >= BN ? BN / 32 : (rem_cols + 31) / 32;
+      const int ngroups = rem_cols >= BN ? BN / kEG : (rem_cols + kEG - 1) / kEG;
       // residual blocks of the first two groups (later ones after each use)
       if (p.res && et == 0) {
-        for (int g = 0; g < 2 && g < ngroups; ++g) issue_res(grp + g, nt * BN + g * 32, m0, b);
+        for (int g = 0; g < 2 && g < ngroups; ++g) issue_res(grp + g, nt * BN + g * kEG, m0, b);
       }
       const int nch = L::kPromote ? (p.num_kb + L::kChunkKB - 1) / L::kChunkKB : 1;
       for (int ch = 0; ch < nch; ++ch) {
@@ -474,7 +490,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // fold the chunk into the running total: each TMEM round trip carries
           // 32 columns of the chunk and 32 of the total (loads issued before
           // one wait), in 16-column pieces to bound live registers
-          const int ncols = ngroups * 32;
+          const int ncols = (ngroups * kEG + 31) / 32 * 32;  // columns < BN
           for (int c = 0; c < ncols; c += 32) {
             uint32_t a0[16], a1[16], b0[16], b1[16];
             tmem_ld_32x32b_x16(tmem_base + lane_addr + ccol + c, a0);
@@ -496,26 +512,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         for (int j = 0; j < ngroups && last; ++j) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(tmem_base + lane_addr + ccol + j * 32, r);
+          uint32_t r[kEG];
+          tmem_ld_cols(tmem_base + lane_addr + ccol + j * kEG, r);
           if (L::kPromote && ch > 0) {
-            uint32_t t[32];
-            tmem_ld_32x32b_x32(tmem_base + lane_addr + j * 32, t);
+            uint32_t t[kEG];
+            tmem_ld_cols(tmem_base + lane_addr + j * kEG, t);
             tmem_ld_wait();
 #pragma unroll
-            for (int e = 0; e < 32; ++e)
+            for (int e = 0; e < kEG; ++e)
               r[e] = __float_as_uint(__uint_as_float(t[e]) + __uint_as_float(r[e]));
           } else {
             tmem_ld_wait();
           }
-          // ---- final values of this 32-column group
-          const int col0 = nt * BN + j * 32;
+          // ---- final values of this group
+          const int col0 = nt * BN + j * kEG;
           const int buf = grp & 1;
-          float v[32];
+          float v[kEG];
 #pragma unroll
-          for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(r[e]);
+          for (int e = 0; e < kEG; ++e) v[e] = __uint_as_float(r[e]);
 #pragma unroll
-          for (int q4 = 0; q4 < 8; ++q4) {
+          for (int q4 = 0; q4 < kEG / 4; ++q4) {
             const int c = col0 + 4 * q4;
             if (c < p.Nc) {
               if (p.scale) {
@@ -533,14 +549,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             w = mbar_wait(res_full(buf), (grp >> 1) & 1, abort_flag, p.status);
             if (w && et == 0) res_out &= ~(1u << buf);
 #pragma unroll
-            for (int q4 = 0; q4 < 8; ++q4) {
-              const float4 rv = ld_shared_f4(res_st + buf * kEpiTile + swz128(et, q4));
+            for (int q4 = 0; q4 < kEG / 4; ++q4) {
+              const float4 rv = ld_shared_f4(res_st + buf * kEpiTile + swz_eg<kEG>(et, q4));
               v[4 * q4] += rv.x; v[4 * q4 + 1] += rv.y; v[4 * q4 + 2] += rv.z; v[4 * q4 + 3] += rv.w;
             }
           }
           if (p.relu) {
 #pragma unroll
-            for (int e = 0; e < 32; ++e) v[e] = v[e] > 0.f ? v[e] : 0.f;
+            for (int e = 0; e < kEG; ++e) v[e] = v[e] > 0.f ? v[e] : 0.f;
           }
           // the staging tile of two groups ago must have been read by its TMA store
           if (et == 0) bulk_wait_group_read<1>();
@@ -548,14 +564,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!ok) break;
           const uint32_t ost = out_st + buf * kEpiTile;
 #pragma unroll
-          for (int q4 = 0; q4 < 8; ++q4)
-            sts_v4(ost + swz128(et, q4), v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
+          for (int q4 = 0; q4 < kEG / 4; ++q4)
+            sts_v4(ost + swz_eg<kEG>(et, q4), v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
           fence_proxy_async_smem();
           named_bar_sync(kEpiThreads);
           if (et == 0) {
             tma_store_3d(&tm_y, col0, m0, b, ost);
             bulk_commit_group();
-            if (p.res && j + 2 < ngroups) issue_res(grp + 2, col0 + 64, m0, b);  // freed buffer
+            if (p.res && j + 2 < ngroups) issue_res(grp + 2, col0 + 2 * kEG, m0, b);  // freed buffer
           }
           ++grp;
         }
@@ -603,54 +619,62 @@ EncodeTiledFn3 tiled_fn() {
 }
 
 // [batches][rows][cols] fp32 output / residual with row stride ld, batch stride
-// bstride (elements); 128 x 32 boxes, 128-byte swizzle.
+// bstride (elements); 128 x eg boxes (eg = 16 or 32 columns, 64- or 128-byte swizzle).
 int encode_out_map(const float* base, int cols, int rows, int batches, int ld, long long bstride,
-                   CUtensorMap* map) {
+                   int eg, CUtensorMap* map) {
   EncodeTiledFn3 fn = tiled_fn();
   if (!fn) return (int)CUDA_ERROR_NOT_FOUND;
   const long long bs = batches > 1 ? bstride : (long long)rows * ld;
   cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)batches};
   cuuint64_t strides[2] = {(cuuint64_t)ld * 4, (cuuint64_t)bs * 4};
-  cuuint32_t box[3] = {32u, (cuuint32_t)kBM, 1u};
+  cuuint32_t box[3] = {(cuuint32_t)eg, (cuuint32_t)kBM, 1u};
   cuuint32_t es[3] = {1u, 1u, 1u};
   return (int)fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box,
-                 es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                 es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                 eg == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
 
-template <int PREC, int BN>
+template <int PREC, int BN, int EG>
 int launch3_t(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap& lo,
               const CUtensorMap& am, int num_sms, cudaStream_t st) {
-  using L = Layout<PREC, BN>;
+  using L = Layout<PREC, BN, EG>;
   static bool attr_set = false;
   if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(igemm_tc3_kernel<PREC, BN>,
+    cudaError_t e = cudaFuncSetAttribute(igemm_tc3_kernel<PREC, BN, EG>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
     if (e != cudaSuccess) return (int)e;
     attr_set = true;
   }
   CUtensorMap ym{}, rm{};
-  int er = encode_out_map(p.y, p.Nc, p.M, p.batches, p.ldy, p.y_bstride, &ym);
+  int er = encode_out_map(p.y, p.Nc, p.M, p.batches, p.ldy, p.y_bstride, EG, &ym);
   if (er) return (int)cudaErrorInvalidValue;
   if (p.res) {
-    er = encode_out_map(p.res, p.Nc, p.M, p.batches, p.ldr, p.y_bstride, &rm);
+    er = encode_out_map(p.res, p.Nc, p.M, p.batches, p.ldr, p.y_bstride, EG, &rm);
     if (er) return (int)cudaErrorInvalidValue;
   }
   const int total = p.m_tiles * p.n_tiles * p.batches;
   const int grid = total < num_sms ? total : num_sms;
   if (grid <= 0) return 0;
-  igemm_tc3_kernel<PREC, BN><<<grid, kThreads, L::kBytes, st>>>(p, hi, lo, am, ym, rm);
+  igemm_tc3_kernel<PREC, BN, EG><<<grid, kThreads, L::kBytes, st>>>(p, hi, lo, am, ym, rm);
   return (int)cudaGetLastError();
 }
 
 }  // namespace
 
+constexpr int kLongK = 16;  // k-blocks (K >= 512)
+
 int igemm3_launch(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap& lo,
                   const CUtensorMap& am, int precision, int bn, int num_sms, cudaStream_t st) {
-  if (precision == kPrec3xTF32 && bn == 64) return launch3_t<kPrec3xTF32, 64>(p, hi, lo, am, num_sms, st);
-  if (precision == kPrec3xTF32 && bn == 128) return launch3_t<kPrec3xTF32, 128>(p, hi, lo, am, num_sms, st);
-  if (precision == kPrecTF32 && bn == 64) return launch3_t<kPrecTF32, 64>(p, hi, lo, am, num_sms, st);
-  if (precision == kPrecTF32 && bn == 128) return launch3_t<kPrecTF32, 128>(p, hi, lo, am, num_sms, st);
+  // 3xTF32, BN = 128: 16-column epilogue groups buy a fourth operand stage,
+  // worth it once the K loop of a tile is long (short-K layers are bound by
+  // their epilogue, which 32-column groups store faster)
+  if (precision == kPrec3xTF32 && bn == 64) return launch3_t<kPrec3xTF32, 64, 32>(p, hi, lo, am, num_sms, st);
+  if (precision == kPrec3xTF32 && bn == 128)
+    return p.num_kb >= kLongK ? launch3_t<kPrec3xTF32, 128, 16>(p, hi, lo, am, num_sms, st)
+                              : launch3_t<kPrec3xTF32, 128, 32>(p, hi, lo, am, num_sms, st);
+  if (precision == kPrecTF32 && bn == 64) return launch3_t<kPrecTF32, 64, 32>(p, hi, lo, am, num_sms, st);
+  if (precision == kPrecTF32 && bn == 128) return launch3_t<kPrecTF32, 128, 32>(p, hi, lo, am, num_sms, st);
   return (int)cudaErrorInvalidValue;
 }
 
