@@ -88,7 +88,9 @@ struct Layout {
   // drain
   static constexpr int kNumBars = 2 * kS1 + kS2 + 7;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
-  static constexpr int kBytes = kOffMisc + 16 + 1024;
+  static constexpr int kOffSS = (kOffMisc + 16 + 127) / 128 * 128;  // scale[BN], shift[BN]
+  static_assert(kOffSS % 16 == 0, "float4 reads of the staged scale / shift");
+  static constexpr int kBytes = kOffSS + 2 * BN * 4 + 1024;
   static_assert(kBytes <= 227 * 1024, "exceeds the 227 KB of shared memory per block");
 };
 
@@ -136,6 +138,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t drain_bar = bar0 + 8u * (2 * S1 + S2 + 6);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + L::kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + L::kOffMisc + 4);
+  float* ss_scale = reinterpret_cast<float*>(gbase + L::kOffSS);
+  float* ss_shift = ss_scale + BN;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -473,6 +477,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int m0 = mt * kBM;
       const int rem_cols = p.Nc - nt * BN;
       const int ngroups = rem_cols >= BN ? BN / kEG : (rem_cols + kEG - 1) / kEG;
+      // this tile's per-channel scale / shift, staged once in shared memory (the
+      // previous tile's last reads happened before its last group barrier)
+      if (p.scale || p.shift) {
+        for (int c = et; c < BN; c += kEpiThreads) {
+          const int gc = nt * BN + c;
+          ss_scale[c] = (p.scale && gc < p.Nc) ? p.scale[gc] : 1.f;
+          ss_shift[c] = (p.shift && gc < p.Nc) ? p.shift[gc] : 0.f;
+        }
+        named_bar_sync(kEpiThreads);
+      }
       // residual blocks of the first two groups (later ones after each use)
       if (p.res && et == 0) {
         for (int g = 0; g < 2 && g < ngroups; ++g) issue_res(grp + g, nt * BN + g * kEG, m0, b);
@@ -532,16 +546,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int e = 0; e < kEG; ++e) v[e] = __uint_as_float(r[e]);
 #pragma unroll
           for (int q4 = 0; q4 < kEG / 4; ++q4) {
-            const int c = col0 + 4 * q4;
-            if (c < p.Nc) {
-              if (p.scale) {
-                const float4 sc = *reinterpret_cast<const float4*>(p.scale + c);
-                v[4 * q4] *= sc.x; v[4 * q4 + 1] *= sc.y; v[4 * q4 + 2] *= sc.z; v[4 * q4 + 3] *= sc.w;
-              }
-              if (p.shift) {
-                const float4 sh = *reinterpret_cast<const float4*>(p.shift + c);
-                v[4 * q4] += sh.x; v[4 * q4 + 1] += sh.y; v[4 * q4 + 2] += sh.z; v[4 * q4 + 3] += sh.w;
-              }
+            const int c = j * kEG + 4 * q4;  // column within the tile
+            if (p.scale) {
+              const float4 sc = *reinterpret_cast<const float4*>(ss_scale + c);
+              v[4 * q4] *= sc.x; v[4 * q4 + 1] *= sc.y; v[4 * q4 + 2] *= sc.z; v[4 * q4 + 3] *= sc.w;
+            }
+            if (p.shift) {
+              const float4 sh = *reinterpret_cast<const float4*>(ss_shift + c);
+              v[4 * q4] += sh.x; v[4 * q4 + 1] += sh.y; v[4 * q4 + 2] += sh.z; v[4 * q4 + 3] += sh.w;
             }
           }
           bool w = true;
