@@ -16,14 +16,19 @@
 //               (2-D tile of the [pixels][channels] matrix for 1x1 stride-1 convs and
 //               GEMMs, or an im2col box for k x k convs: the hardware walks 128 output
 //               pixels across rows and images, zero fill = padding) and the weight
-//               tiles.  Gather mode (channel counts not a multiple of 16, e.g. the RGB
-//               stem): 16-byte cp.async copies with zero fill.
-//   warps 8-11  converters: warp 8+q owns TMEM lanes 32q..32q+31 (= tile rows); each
-//               thread reads its row of the raw fp32 stage, rounds (TF32) or splits
-//               (3xTF32: hi = rna(v), lo = rna(v - hi)) and writes it to a TMEM A stage.
-//   warp 12     TMEM allocation and single-thread tcgen05.mma (kind::tf32, A from
-//               TMEM, B from shared memory).
-// 3xTF32: a*b ~= a_hi*b_hi + a_hi*b_lo + a_lo*b_hi (Ootomo & Yokota, 2022).  The
+//               tiles.  Taps mode (4, 8 or 16 channels): one im2col box per filter
+//               tap.  Gather mode (other channel counts): 16-byte cp.async copies
+//               with zero fill.
+//   warps 8-11  converters: warp 8+q owns TMEM lanes 32q..32q+31 (= tile rows).  The
+//               MMAs read the raw fp32 A from shared memory as its tf32 hi part (the
+//               tensor core uses the upper 19 bits); in 3xTF32 each thread computes
+//               lo = rna(v - trunc(v)) for its row and writes it to a TMEM A stage.
+//               The stage itself is only rewritten to lay taps-mode boxes out for
+//               the MMA or to zero K padding.
+//   warp 12     TMEM allocation and single-thread tcgen05.mma (kind::tf32; A hi and B
+//               from shared memory, A lo from TMEM).
+// 3xTF32: a*b ~= a_hi*b_hi + a_hi*b_lo + a_lo*b_hi (Ootomo & Yokota, 2022), here with
+// hi = the truncated tf32 and lo = the rounded remainder, for both operands.  The
 // tensor core adds into its fp32 accumulator with truncation, so each TMEM
 // accumulator sums only 4 k-blocks (48 MMAs) and the epilogue warps fold these
 // chunks into a running total with round-to-nearest fp32 adds.
@@ -66,12 +71,11 @@ struct Layout {
   static constexpr bool kPromote = kSplit;
   static constexpr int kChunkKB = kPromote ? 4 : (1 << 30);  // 48 MMAs per chunk
   static constexpr int kAccCols = kPromote ? 3 * BN : 2 * BN;
-  // TMEM A stage: the hi half only (3xTF32); the lo half (and TF32's rounded
-  // A) overwrites the raw A in shared memory and is read from there
+  // TMEM A stage: the lo half (3xTF32); the hi half is the raw A in shared memory
   static constexpr int kAStageCols = kSplit ? kBK : 0;
   static constexpr int kS2raw = kSplit ? (512 - kAccCols) / kBK : 64;
-  // One ring: stage s holds raw A + B in shared memory and A hi/lo in TMEM, so a
-  // single barrier per stage tracks its release (converters + one MMA commit).
+  // One ring: stage s holds raw A + B in shared memory and A lo in TMEM, so a
+  // single barrier per stage (one MMA commit) tracks its release.
   static constexpr int kS1 = kS1cap < kS2raw ? kS1cap : kS2raw;
   static constexpr int kS2 = kS1;
   static_assert(kS2 >= 2, "TMEM too small for two A stages");
@@ -324,8 +328,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int a = item % S2;
       bool ok = mbar_wait(s1_full(s), (item / S1) & 1, abort_flag, p.status);
       const uint32_t rbase = a_raw + s * L::kARaw;
+      // k beyond K: padding of the last k-block (zero weights); never multiply
+      // whatever the stage held there
+      const int kvalid = p.K - kb * kBK;
+      if (++kb == p.num_kb) kb = 0;
+      // The MMAs read the raw fp32 A from shared memory as its tf32 hi part
+      // (the tensor core ignores the 13 low mantissa bits).  The stage is only
+      // rewritten here when its layout is not the MMA's (taps mode) or when
+      // padding must be zeroed.
+      const bool rewrite = taps || kvalid < kBK;
       float v[kBK];
-      if (ok) {
+      if (ok && (L::kSplit || rewrite)) {
 #pragma unroll
         for (int c = 0; c < kBK / 4; ++c) {
           const float4 f = ld_shared_f4(rbase + coff[c]);
@@ -339,41 +352,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       // read its row before any writes (the AND keeps an abort uniform)
       if (taps) ok = named_bar_and(ok, 128, 2);
       if (!ok) break;
-      // k beyond K: padding of the last k-block (zero weights); never multiply
-      // whatever the stage held there
-      const int kvalid = p.K - kb * kBK;
-      if (kvalid < kBK) {
+      if (rewrite) {
+        if (kvalid < kBK) {
 #pragma unroll
-        for (int e = 0; e < kBK; ++e)
-          if (e >= kvalid) v[e] = 0.f;
-      }
-      if (++kb == p.num_kb) kb = 0;
-      uint32_t hi[kBK];
-#pragma unroll
-      for (int e = 0; e < kBK; ++e) hi[e] = __float_as_uint(to_tf32(v[e]));
-      if constexpr (L::kSplit) {
-        // lo = rna(v - hi) in place of the raw row (128-byte swizzled, the layout
-        // the MMA's shared-memory descriptor reads); hi to this stage's TMEM slot,
-        // which is free: the loader refilled the stage only after the MMAs of its
-        // previous use committed, and this thread has seen the refill land
-#pragma unroll
-        for (int c = 0; c < kBK / 4; ++c) {
-          float l[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) l[e] = to_tf32(v[4 * c + e] - __uint_as_float(hi[4 * c + e]));
-          st_shared_f4(rbase + swz128(row, c), l[0], l[1], l[2], l[3]);
+          for (int e = 0; e < kBK; ++e)
+            if (e >= kvalid) v[e] = 0.f;
         }
-        tc_fence_after();
-        tmem_st_32x32b_x32(tmem_base + lane_addr + L::kACol0 + a * L::kAStageCols, hi);
-        tmem_st_wait();
-        tc_fence_before();
-      } else {
 #pragma unroll
         for (int c = 0; c < kBK / 4; ++c)
-          st_shared_f4(rbase + swz128(row, c), __uint_as_float(hi[4 * c]), __uint_as_float(hi[4 * c + 1]),
-                       __uint_as_float(hi[4 * c + 2]), __uint_as_float(hi[4 * c + 3]));
+          st_shared_f4(rbase + swz128(row, c), v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
       }
-      fence_proxy_async_smem();  // the generic-proxy stores, visible to the tensor core
+      if constexpr (L::kSplit) {
+        // lo = rna(v - trunc(v)) to this stage's TMEM slot, which is free: the
+        // loader refilled the stage only after the MMAs of its previous use
+        // committed, and this thread has seen the refill land
+        uint32_t lo[kBK];
+#pragma unroll
+        for (int e = 0; e < kBK; ++e) lo[e] = __float_as_uint(to_tf32(v[e] - tf32_trunc(v[e])));
+        tc_fence_after();
+        tmem_st_32x32b_x32(tmem_base + lane_addr + L::kACol0 + a * L::kAStageCols, lo);
+        tmem_st_wait();
+        tc_fence_before();
+      }
+      if (rewrite) fence_proxy_async_smem();  // the generic-proxy stores, visible to the tensor core
       mbar_arrive(t_full(a));
     }
   } else if (warp == kMmaWarp) {
@@ -414,8 +415,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         if (lane == 0) {
-          const uint32_t ahi = tmem_base + L::kACol0 + a * L::kAStageCols;
-          const uint64_t da = smem_desc_sw128(a_raw + s * L::kARaw);  // A lo (TF32: A)
+          const uint32_t alo = tmem_base + L::kACol0 + a * L::kAStageCols;  // A lo (TMEM)
+          const uint64_t da = smem_desc_sw128(a_raw + s * L::kARaw);          // A (hi: raw fp32)
           const uint64_t dbh = smem_desc_sw128(b_hi + s * L::kBBytes);
           uint64_t dbl = 0;
           if constexpr (L::kSplit) dbl = smem_desc_sw128(b_lo + s * L::kBBytes);
@@ -423,9 +424,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int kk = 0; kk < kBK / 8; ++kk) {
             const uint32_t acc = ((L::kPromote ? kin : kb) | kk) ? 1u : 0u;
             if constexpr (L::kSplit) {
-              tc_mma_tf32_ts(d_tmem, ahi + kk * 8, dbh + (uint64_t)(kk * 2), idesc, acc);
-              tc_mma_tf32_ts(d_tmem, ahi + kk * 8, dbl + (uint64_t)(kk * 2), idesc, 1u);
-              tc_mma<0>(d_tmem, da + (uint64_t)(kk * 2), dbh + (uint64_t)(kk * 2), idesc, 1u);
+              tc_mma<0>(d_tmem, da + (uint64_t)(kk * 2), dbh + (uint64_t)(kk * 2), idesc, acc);
+              tc_mma<0>(d_tmem, da + (uint64_t)(kk * 2), dbl + (uint64_t)(kk * 2), idesc, 1u);
+              tc_mma_tf32_ts(d_tmem, alo + kk * 8, dbh + (uint64_t)(kk * 2), idesc, 1u);
             } else {
               tc_mma<0>(d_tmem, da + (uint64_t)(kk * 2), dbh + (uint64_t)(kk * 2), idesc, acc);
             }

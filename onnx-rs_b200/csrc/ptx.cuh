@@ -362,4 +362,10 @@ __device__ __forceinline__ float to_tf32(float x) {
   return __uint_as_float(r);
 }
 
+// fp32 -> tf32 by truncation (the 13 low mantissa bits cleared): the value a
+// kind::tf32 MMA operand takes when its 32-bit container holds a full fp32.
+__device__ __forceinline__ float tf32_trunc(float x) {
+  return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+}
+
 }  // namespace ob2

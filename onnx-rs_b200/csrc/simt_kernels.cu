@@ -170,10 +170,15 @@ __global__ void pack_b_kernel(const float* __restrict__ src, int rows, int K, in
       reinterpret_cast<__nv_bfloat16*>(hi)[i] = __float2bfloat16_rn(v);
     } else if (prec == kPrecFP32) {
       reinterpret_cast<float*>(hi)[i] = v;
-    } else {
-      const float h = to_tf32(v);
+    } else if (prec == kPrec3xTF32) {
+      // hi = the truncated tf32 the tensor core reads from an fp32 container,
+      // lo = the remainder rounded to tf32 (the activations are split the same
+      // way on the fly)
+      const float h = tf32_trunc(v);
       reinterpret_cast<float*>(hi)[i] = h;
-      if (prec == kPrec3xTF32) reinterpret_cast<float*>(lo)[i] = to_tf32(v - h);
+      reinterpret_cast<float*>(lo)[i] = to_tf32(v - h);
+    } else {
+      reinterpret_cast<float*>(hi)[i] = to_tf32(v);
     }
   }
 }
