@@ -34,6 +34,13 @@ sys.path.insert(0, ROOT)
 GLOBAL_BATCH = 256
 SEED = 4
 METRIC = "ResNet-50 v1.5 images/sec (batch 256, fp32 via 3xTF32)"
+METRIC_FAST = {"tf32": "ResNet-50 v1.5 images/sec (batch 256, fast mode: 1xTF32)",
+               "bf16": "ResNet-50 v1.5 images/sec (batch 256, fast mode: BF16)",
+               "fp32": "ResNet-50 v1.5 images/sec (batch 256, fp32 on CUDA cores)"}
+# DRAM bytes per igemm_tc3_kernel launch, mean over the 53 launches of one
+# batch-256 3xTF32 run: ncu dram__bytes_read.sum + dram__bytes_write.sum
+# (profiles/resnet50_b256_launch_list.md).
+TRAFFIC_PER_LAUNCH_3XTF32 = 472.2e6
 L2_BYTES = 126 * 1024 * 1024
 
 
@@ -392,8 +399,12 @@ def main():
         basis = "fp32 CUDA cores compared against tf32 dense"
     n_tc_launch = len(tc)
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                "frac": achieved / peak if peak else None, "traffic": None,
-                "kernel": "igemm_tc_kernel (all Conv/Gemm launches of one run)",
+                "frac": achieved / peak if peak else None,
+                "traffic": TRAFFIC_PER_LAUNCH_3XTF32 if args.precision == "3xtf32" and args.batch == 256 else None,
+                "traffic_note": "DRAM bytes per conv launch from one ncu capture of this workload"
+                                " (bytes, mean over the run's launches)",
+                "kernel": ("igemm_tc_kernel" if args.precision == "bf16" else "igemm_tc3_kernel")
+                + " (all Conv/Gemm launches of one run)",
                 "launches": n_tc_launch, "flops_per_launch": tc_flops / max(1, n_tc_launch),
                 "peak_source": f"{peak_src}: {basis}",
                 "frac_of_raw_tf32": (3 * achieved / (bf16 / 2.0)) if args.precision == "3xtf32" else None}
@@ -407,7 +418,8 @@ def main():
         if world == 1 and not args.no_cpu_baseline:
             cpu = cpu_baseline(steps=1)
         line = {
-            "metric": METRIC, "value": value, "unit": "images/s", "n_gpus": world, "steps": args.steps,
+            "metric": METRIC if args.precision == "3xtf32" else METRIC_FAST[args.precision],
+            "value": value, "unit": "images/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32" if args.precision in ("3xtf32", "fp32") else args.precision,
             "precision": args.precision, "data": "synthetic",
