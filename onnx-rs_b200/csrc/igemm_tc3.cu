@@ -71,14 +71,17 @@ struct Layout {
   static constexpr bool kPromote = kSplit;
   static constexpr int kChunkKB = kPromote ? 4 : (1 << 30);  // 48 MMAs per chunk
   static constexpr int kAccCols = kPromote ? 3 * BN : 2 * BN;
-  // TMEM A stage: the lo half (3xTF32); the hi half is the raw A in shared memory
-  static constexpr int kAStageCols = kSplit ? kBK : 0;
-  static constexpr int kS2raw = kSplit ? (512 - kAccCols) / kBK : 64;
-  // One ring: stage s holds raw A + B in shared memory and A lo in TMEM, so a
-  // single barrier per stage (one MMA commit) tracks its release.
-  static constexpr int kS1 = kS1cap < kS2raw ? kS1cap : kS2raw;
-  static constexpr int kS2 = kS1;
-  static_assert(kS2 >= 2, "TMEM too small for two A stages");
+  // 3xTF32: every MMA reads A from TMEM (a slot = hi[32] | lo[32] columns), so
+  // shared memory serves only the B operands to the tensor core -- the kernel is
+  // bound by shared-memory bandwidth (128 B/cycle/SM), which the A reads of
+  // A-from-shared-memory MMAs would take.  The TMEM slots form their own ring
+  // (S2 <= S1), reused once the commit of the slot's previous item has fired.
+  // TF32: A is read from shared memory as it landed; S2 == S1, no TMEM slots.
+  static constexpr int kAStageCols = kSplit ? 2 * kBK : 0;
+  static constexpr int kS2raw = kSplit ? (512 - kAccCols) / kAStageCols : 64;
+  static constexpr int kS1 = kS1cap;
+  static constexpr int kS2 = (kSplit && kS2raw < kS1) ? kS2raw : kS1;
+  static_assert(kS2 >= 2, "TMEM too small for two A slots");
   static_assert(kS1 >= 3, "shared memory too small");
   static constexpr int kACol0 = kAccCols;
   static constexpr int kTmemCols = 512;
@@ -332,11 +335,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       // whatever the stage held there
       const int kvalid = p.K - kb * kBK;
       if (++kb == p.num_kb) kb = 0;
-      // The MMAs read the raw fp32 A from shared memory as its tf32 hi part
-      // (the tensor core ignores the 13 low mantissa bits).  The stage is only
-      // rewritten here when its layout is not the MMA's (taps mode) or when
-      // padding must be zeroed.
-      const bool rewrite = taps || kvalid < kBK;
+      // TF32: the MMAs read the raw fp32 A from shared memory (the tensor core
+      // uses the upper 19 bits of the container); the stage is only rewritten
+      // when its layout is not the MMA's (taps mode) or padding must be zeroed.
+      // 3xTF32: A goes to TMEM, so its shared-memory layout does not matter.
+      const bool rewrite = !L::kSplit && (taps || kvalid < kBK);
       float v[kBK];
       if (ok && (L::kSplit || rewrite)) {
 #pragma unroll
@@ -350,27 +353,37 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // taps mode rewrites the stage in another layout: every converter has
       // read its row before any writes (the AND keeps an abort uniform)
-      if (taps) ok = named_bar_and(ok, 128, 2);
+      if (!L::kSplit && taps) ok = named_bar_and(ok, 128, 2);
       if (!ok) break;
-      if (rewrite) {
-        if (kvalid < kBK) {
+      if (kvalid < kBK) {
 #pragma unroll
-          for (int e = 0; e < kBK; ++e)
-            if (e >= kvalid) v[e] = 0.f;
-        }
+        for (int e = 0; e < kBK; ++e)
+          if (e >= kvalid) v[e] = 0.f;
+      }
+      if (rewrite) {
 #pragma unroll
         for (int c = 0; c < kBK / 4; ++c)
           st_shared_f4(rbase + swz128(row, c), v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
       }
       if constexpr (L::kSplit) {
-        // lo = rna(v - trunc(v)) to this stage's TMEM slot, which is free: the
-        // loader refilled the stage only after the MMAs of its previous use
-        // committed, and this thread has seen the refill land
-        uint32_t lo[kBK];
+        // hi = trunc_tf32(v), lo = rna_tf32(v - hi) into TMEM slot a, once the
+        // MMAs of the slot's previous use (item - S2) have completed: their
+        // commit is the one that freed that item's shared-memory stage.  No
+        // parity ambiguity: the refill this thread saw on s1_full needed the
+        // commit of item - S1, and commits complete in order.
+        if (item >= S2) {
+          const int prev = item - S2;
+          if (!mbar_wait(s1_empty(prev % S1), (prev / S1) & 1, abort_flag, p.status)) break;
+        }
+        uint32_t hl[kBK];
 #pragma unroll
-        for (int e = 0; e < kBK; ++e) lo[e] = __float_as_uint(to_tf32(v[e] - tf32_trunc(v[e])));
+        for (int e = 0; e < kBK; ++e) hl[e] = __float_as_uint(tf32_trunc(v[e]));
         tc_fence_after();
-        tmem_st_32x32b_x32(tmem_base + lane_addr + L::kACol0 + a * L::kAStageCols, lo);
+        const uint32_t slot = tmem_base + lane_addr + L::kACol0 + a * L::kAStageCols;
+        tmem_st_32x32b_x32(slot, hl);
+#pragma unroll
+        for (int e = 0; e < kBK; ++e) hl[e] = __float_as_uint(to_tf32(v[e] - tf32_trunc(v[e])));
+        tmem_st_32x32b_x32(slot + kBK, hl);
         tmem_st_wait();
         tc_fence_before();
       }
@@ -379,80 +392,68 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
+    // One thread, one flat loop over this CTA's k-blocks with incremental ring
+    // indices: the MMA issue rate of this thread bounds the kernel.
     constexpr uint32_t idesc = make_idesc(2, kBM, BN);
-    int item = 0;
-    bool issued = false;
-    uint32_t cc = 0;
-    for (int tj = 0; tj < my_tiles; ++tj) {
-      const int buf = tj & 1;
-      uint32_t d_tmem = tmem_base + buf * BN;
-      int cb = 0;
-      if constexpr (!L::kPromote) {
-        if (!mbar_wait(acc_empty(buf), ((tj >> 1) & 1) ^ 1, abort_flag, p.status)) break;
-        tc_fence_after();
-      }
-      bool failed = false;
-      for (int kb = 0; kb < p.num_kb; ++kb, ++item) {
-        const int s = item % S1;
-        const int a = item % S2;
-        const int kin = kb % L::kChunkKB;
-        if constexpr (L::kPromote) {
-          if (kin == 0) {
-            cb = cc & 1;
-            if (!mbar_wait(acc_empty(cb), ((cc >> 1) & 1) ^ 1, abort_flag, p.status)) {
-              failed = true;
-              break;
-            }
-            tc_fence_after();
-            d_tmem = tmem_base + BN * (1 + cb);
-          }
+    if (lane == 0) {
+      bool issued = false;
+      uint32_t cc = 0;             // accumulation units started (chunks / tiles)
+      int s = 0, a = 0;            // shared-memory stage, TMEM A slot
+      uint32_t pa = 0;             // parity of slot a's current use
+      int kb = 0, kin = 0, cb = 0;  // k-block in the tile / in the accumulation unit
+      uint32_t d_tmem = tmem_base;
+      for (int item = 0; item < total_items; ++item) {
+        if (kin == 0) {
+          cb = cc & 1;
+          if (!mbar_wait(acc_empty(cb), ((cc >> 1) & 1) ^ 1, abort_flag, p.status)) break;
+          d_tmem = tmem_base + BN * (L::kPromote ? 1 + cb : cb);
         }
-        // one wait per stage: the converters arrive on t_full only after they
-        // saw the stage's TMA (A and B) complete on s1_full
-        if (!mbar_wait(t_full(a), (item / S2) & 1, abort_flag, p.status)) {
-          failed = true;
-          break;
-        }
+        // the converters arrive on t_full only after they saw the stage's TMA
+        // (A and B) complete on s1_full and wrote its A operands
+        if (!mbar_wait(t_full(a), pa, abort_flag, p.status)) break;
         tc_fence_after();
-        if (lane == 0) {
-          const uint32_t alo = tmem_base + L::kACol0 + a * L::kAStageCols;  // A lo (TMEM)
-          const uint64_t da = smem_desc_sw128(a_raw + s * L::kARaw);          // A (hi: raw fp32)
-          const uint64_t dbh = smem_desc_sw128(b_hi + s * L::kBBytes);
-          uint64_t dbl = 0;
-          if constexpr (L::kSplit) dbl = smem_desc_sw128(b_lo + s * L::kBBytes);
+        const uint32_t ahi = tmem_base + L::kACol0 + a * L::kAStageCols;  // 3xTF32: A hi | lo
+        const uint32_t alo = ahi + kBK;
+        const uint64_t da = smem_desc_sw128(a_raw + s * L::kARaw);  // TF32: A as landed
+        const uint64_t dbh = smem_desc_sw128(b_hi + s * L::kBBytes);
+        uint64_t dbl = 0;
+        if constexpr (L::kSplit) dbl = smem_desc_sw128(b_lo + s * L::kBBytes);
 #pragma unroll
-          for (int kk = 0; kk < kBK / 8; ++kk) {
-            const uint32_t acc = ((L::kPromote ? kin : kb) | kk) ? 1u : 0u;
-            if constexpr (L::kSplit) {
-              tc_mma<0>(d_tmem, da + (uint64_t)(kk * 2), dbh + (uint64_t)(kk * 2), idesc, acc);
-              tc_mma<0>(d_tmem, da + (uint64_t)(kk * 2), dbl + (uint64_t)(kk * 2), idesc, 1u);
-              tc_mma_tf32_ts(d_tmem, alo + kk * 8, dbh + (uint64_t)(kk * 2), idesc, 1u);
-            } else {
-              tc_mma<0>(d_tmem, da + (uint64_t)(kk * 2), dbh + (uint64_t)(kk * 2), idesc, acc);
-            }
-          }
-          tc_commit(s1_empty(s));  // frees the stage: shared memory and TMEM A slot
-          issued = true;
-        }
-        if constexpr (L::kPromote) {
-          if (kin == L::kChunkKB - 1 || kb == p.num_kb - 1) {
-            if (lane == 0) tc_commit(acc_full(cb));
-            ++cc;
+        for (int kk = 0; kk < kBK / 8; ++kk) {
+          const uint32_t acc = (kin | kk) ? 1u : 0u;
+          if constexpr (L::kSplit) {
+            tc_mma_tf32_ts(d_tmem, ahi + kk * 8, dbh + (uint64_t)(kk * 2), idesc, acc);
+            tc_mma_tf32_ts(d_tmem, ahi + kk * 8, dbl + (uint64_t)(kk * 2), idesc, 1u);
+            tc_mma_tf32_ts(d_tmem, alo + kk * 8, dbh + (uint64_t)(kk * 2), idesc, 1u);
+          } else {
+            tc_mma<0>(d_tmem, da + (uint64_t)(kk * 2), dbh + (uint64_t)(kk * 2), idesc, acc);
           }
         }
-        __syncwarp();
+        // frees the shared-memory stage (and, through it, the TMEM A slot: the
+        // converters wait for this commit before refilling the slot)
+        tc_commit(s1_empty(s));
+        issued = true;
+        const bool tile_end = ++kb == p.num_kb;
+        if (tile_end) kb = 0;
+        if (tile_end || (L::kPromote && kin + 1 == L::kChunkKB)) {
+          tc_commit(acc_full(cb));
+          ++cc;
+          kin = 0;
+        } else {
+          ++kin;
+        }
+        if (++s == S1) s = 0;
+        if (++a == S2) {
+          a = 0;
+          pa ^= 1;
+        }
       }
-      if (failed) break;
-      if constexpr (!L::kPromote) {
-        if (lane == 0) tc_commit(acc_full(buf));
+      // every MMA issued by this thread completes before TMEM is freed
+      if (issued) {
+        tc_commit(drain_bar);
+        volatile int no_abort = 0;
+        mbar_wait(drain_bar, 0, &no_abort, p.status);
       }
-      __syncwarp();
-    }
-    // every MMA issued by this thread completes before TMEM is freed
-    if (lane == 0 && issued) {
-      tc_commit(drain_bar);
-      volatile int no_abort = 0;
-      mbar_wait(drain_bar, 0, &no_abort, p.status);
     }
     __syncwarp();
   } else {
