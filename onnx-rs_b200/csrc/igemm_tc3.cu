@@ -70,7 +70,14 @@ struct Layout {
   static constexpr int kS1cap = kS1raw > 8 ? 8 : kS1raw;
   static constexpr bool kPromote = kSplit;
   static constexpr int kChunkKB = kPromote ? 4 : (1 << 30);  // 48 MMAs per chunk
-  static constexpr int kAccCols = kPromote ? 3 * BN : 2 * BN;
+  // 3xTF32 with BN = 64: B hi and B lo sit back to back in each stage, so one
+  // N = 128 MMA computes [a_hi.b_hi | a_hi.b_lo] and an N = 64 MMA adds a_lo.b_hi
+  // to the second half: two MMA instructions per K step instead of three (the
+  // MMA issue rate of one thread bounds the kernel).  Chunk accumulators are
+  // then 128 columns wide (big | small terms), 128-column aligned.
+  static constexpr bool kStack = kSplit && BN == 64;
+  static constexpr int kChunkCols = kStack ? 128 : BN;
+  static constexpr int kAccCols = kPromote ? (kStack ? 384 : 3 * BN) : 2 * BN;
   // 3xTF32: every MMA reads A from TMEM (a slot = hi[32] | lo[32] columns), so
   // shared memory serves only the B operands to the tensor core -- the kernel is
   // bound by shared-memory bandwidth (128 B/cycle/SM), which the A reads of
@@ -89,8 +96,9 @@ struct Layout {
   static constexpr int kOffRes = 2 * kEpiTile;          // res[2]
   static constexpr int kOffA = 4 * kEpiTile;            // raw A stages
   static constexpr int kOffB = kOffA + kS1 * kARaw;     // B hi stages
-  static constexpr int kOffBlo = kOffB + kS1 * kBBytes;  // B lo stages
-  static constexpr int kOffBar = kOffBlo + (kSplit ? kS1 * kBBytes : 0);
+  static constexpr int kBStride = (kStack ? 2 : 1) * kBBytes;  // stage s at kOffB + s * kBStride
+  static constexpr int kOffBlo = kStack ? kOffB + kBBytes : kOffB + kS1 * kBBytes;  // B lo stages
+  static constexpr int kOffBar = kOffB + kS1 * kBBytes + (kSplit ? kS1 * kBBytes : 0);
   // s1_full[S1], s1_empty[S1], t_full[S2], acc_full[2], acc_empty[2], res_full[2],
   // drain
   static constexpr int kNumBars = 2 * kS1 + kS2 + 7;
@@ -241,8 +249,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           const int brow = nt * BN + (p.b_row ? p.b_row[b] : 0);
-          tma_load_2d(b_hi + s * L::kBBytes, &tm_hi, k0, brow, s1_full(s));
-          if (L::kSplit) tma_load_2d(b_lo + s * L::kBBytes, &tm_lo, k0, brow, s1_full(s));
+          tma_load_2d(b_hi + s * L::kBStride, &tm_hi, k0, brow, s1_full(s));
+          if (L::kSplit) tma_load_2d(b_lo + s * L::kBStride, &tm_lo, k0, brow, s1_full(s));
         }
       }
     } else {
@@ -284,8 +292,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lt == 0) {
           const int brow = nt * BN + (p.b_row ? p.b_row[b] : 0);
           mbar_expect_tx(s1_full(s), (L::kSplit ? 2 : 1) * L::kBBytes);
-          tma_load_2d(b_hi + s * L::kBBytes, &tm_hi, kb * kBK, brow, s1_full(s));
-          if (L::kSplit) tma_load_2d(b_lo + s * L::kBBytes, &tm_lo, kb * kBK, brow, s1_full(s));
+          tma_load_2d(b_hi + s * L::kBStride, &tm_hi, kb * kBK, brow, s1_full(s));
+          if (L::kSplit) tma_load_2d(b_lo + s * L::kBStride, &tm_lo, kb * kBK, brow, s1_full(s));
         }
         const int k = kb * kBK + chunk * 4;
         int dy = 0, dx = 0, ci = 0;
@@ -395,6 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // One thread, one flat loop over this CTA's k-blocks with incremental ring
     // indices: the MMA issue rate of this thread bounds the kernel.
     constexpr uint32_t idesc = make_idesc(2, kBM, BN);
+    constexpr uint32_t idesc2 = make_idesc(2, kBM, 2 * BN);  // stacked B (BN = 64)
     if (lane == 0) {
       bool issued = false;
       uint32_t cc = 0;             // accumulation units started (chunks / tiles)
@@ -406,7 +415,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (kin == 0) {
           cb = cc & 1;
           if (!mbar_wait(acc_empty(cb), ((cc >> 1) & 1) ^ 1, abort_flag, p.status)) break;
-          d_tmem = tmem_base + BN * (L::kPromote ? 1 + cb : cb);
+          d_tmem = tmem_base + (L::kPromote ? L::kChunkCols * (1 + cb) : BN * cb);
         }
         // the converters arrive on t_full only after they saw the stage's TMA
         // (A and B) complete on s1_full and wrote its A operands
@@ -415,13 +424,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t ahi = tmem_base + L::kACol0 + a * L::kAStageCols;  // 3xTF32: A hi | lo
         const uint32_t alo = ahi + kBK;
         const uint64_t da = smem_desc_sw128(a_raw + s * L::kARaw);  // TF32: A as landed
-        const uint64_t dbh = smem_desc_sw128(b_hi + s * L::kBBytes);
+        const uint64_t dbh = smem_desc_sw128(b_hi + s * L::kBStride);
         uint64_t dbl = 0;
-        if constexpr (L::kSplit) dbl = smem_desc_sw128(b_lo + s * L::kBBytes);
+        if constexpr (L::kSplit) dbl = smem_desc_sw128(b_lo + s * L::kBStride);
 #pragma unroll
         for (int kk = 0; kk < kBK / 8; ++kk) {
           const uint32_t acc = (kin | kk) ? 1u : 0u;
-          if constexpr (L::kSplit) {
+          if constexpr (L::kStack) {
+            // [hi.b_hi | hi.b_lo] over B hi and B lo rows, then lo.b_hi into the
+            // second (small-term) half
+            tc_mma_tf32_ts(d_tmem, ahi + kk * 8, dbh + (uint64_t)(kk * 2), idesc2, acc);
+            tc_mma_tf32_ts(d_tmem + BN, alo + kk * 8, dbh + (uint64_t)(kk * 2), idesc, 1u);
+          } else if constexpr (L::kSplit) {
             tc_mma_tf32_ts(d_tmem, ahi + kk * 8, dbh + (uint64_t)(kk * 2), idesc, acc);
             tc_mma_tf32_ts(d_tmem, ahi + kk * 8, dbl + (uint64_t)(kk * 2), idesc, 1u);
             tc_mma_tf32_ts(d_tmem, alo + kk * 8, dbh + (uint64_t)(kk * 2), idesc, 1u);
@@ -501,8 +515,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         tc_fence_after();
         const bool last = ch == nch - 1;
-        const uint32_t ccol = L::kPromote ? BN * (1 + cb) : cb * BN;  // accumulator columns
-        if (L::kPromote && !last) {
+        const uint32_t ccol = L::kPromote ? L::kChunkCols * (1 + cb) : cb * BN;  // accumulator columns
+        if (L::kStack && !last) {
+          // total += big + small, 16 columns at a time
+          for (int c = 0; c < BN; c += 16) {
+            uint32_t a0[16], s0[16], b0[16];
+            tmem_ld_32x32b_x16(tmem_base + lane_addr + ccol + c, a0);
+            tmem_ld_32x32b_x16(tmem_base + lane_addr + ccol + BN + c, s0);
+            if (ch > 0) tmem_ld_32x32b_x16(tmem_base + lane_addr + c, b0);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              float v = __uint_as_float(a0[e]) + __uint_as_float(s0[e]);
+              if (ch > 0) v = __uint_as_float(b0[e]) + v;
+              a0[e] = __float_as_uint(v);
+            }
+            tmem_st_32x32b_x16(tmem_base + lane_addr + c, a0);
+          }
+        } else if (L::kPromote && !last) {
           // fold the chunk into the running total: each TMEM round trip carries
           // 32 columns of the chunk and 32 of the total (loads issued before
           // one wait), in 16-column pieces to bound live registers
@@ -530,6 +560,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < ngroups && last; ++j) {
           uint32_t r[kEG];
           tmem_ld_cols(tmem_base + lane_addr + ccol + j * kEG, r);
+          if constexpr (L::kStack) {  // big + small halves of the chunk
+            uint32_t sm[kEG];
+            tmem_ld_cols(tmem_base + lane_addr + ccol + BN + j * kEG, sm);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < kEG; ++e)
+              r[e] = __float_as_uint(__uint_as_float(r[e]) + __uint_as_float(sm[e]));
+          }
           if (L::kPromote && ch > 0) {
             uint32_t t[kEG];
             tmem_ld_cols(tmem_base + lane_addr + j * kEG, t);
