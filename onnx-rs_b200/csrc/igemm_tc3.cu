@@ -99,9 +99,9 @@ struct Layout {
   static constexpr int kBStride = (kStack ? 2 : 1) * kBBytes;  // stage s at kOffB + s * kBStride
   static constexpr int kOffBlo = kStack ? kOffB + kBBytes : kOffB + kS1 * kBBytes;  // B lo stages
   static constexpr int kOffBar = kOffB + kS1 * kBBytes + (kSplit ? kS1 * kBBytes : 0);
-  // s1_full[S1], s1_empty[S1], t_full[S2], acc_full[2], acc_empty[2], res_full[2],
-  // drain
-  static constexpr int kNumBars = 2 * kS1 + kS2 + 7;
+  // s1_full[S1], s1_empty[S1], t_full[S2], acc_full[2], acc_empty[2],
+  // res_full[4 warps][2], drain
+  static constexpr int kNumBars = 2 * kS1 + kS2 + 13;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kOffSS = (kOffMisc + 16 + 127) / 128 * 128;  // scale[BN], shift[BN]
   static_assert(kOffSS % 16 == 0, "float4 reads of the staged scale / shift");
@@ -149,8 +149,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto t_full = [&](int a) { return bar0 + 8u * (2 * S1 + a); };
   auto acc_full = [&](int b) { return bar0 + 8u * (2 * S1 + S2 + b); };
   auto acc_empty = [&](int b) { return bar0 + 8u * (2 * S1 + S2 + 2 + b); };
-  auto res_full = [&](int b) { return bar0 + 8u * (2 * S1 + S2 + 4 + b); };
-  const uint32_t drain_bar = bar0 + 8u * (2 * S1 + S2 + 6);
+  auto res_full = [&](int w, int b) { return bar0 + 8u * (2 * S1 + S2 + 4 + 2 * w + b); };
+  const uint32_t drain_bar = bar0 + 8u * (2 * S1 + S2 + 12);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + L::kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + L::kOffMisc + 4);
   float* ss_scale = reinterpret_cast<float*>(gbase + L::kOffSS);
@@ -170,7 +170,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int b = 0; b < 2; ++b) {
       mbar_init(acc_full(b), 1);
       mbar_init(acc_empty(b), kEpiThreads);
-      mbar_init(res_full(b), 1);
+      for (int w = 0; w < 4; ++w) mbar_init(res_full(w, b), 1);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -472,29 +472,39 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
+    // Each warp stores (and loads the residual of) its own 32 rows of a group
+    // with its own TMA boxes, so groups need no barrier across the four warps;
+    // the warps agree (barrier AND-reduction) only once per accumulator chunk
+    // and per tile, which also keeps every abort decision uniform.
     const int et = threadIdx.x;  // 0..127 = tile row
     const uint32_t lane_addr = (uint32_t)(warp * 32) << 16;
+    constexpr int kWTile = kEpiTile / 4;  // this warp's 32 rows of a staging tile
     uint32_t cc = 0;   // accumulator chunks consumed
     uint32_t grp = 0;  // kEG-column output groups produced (staging buffer = grp & 1)
     bool ok = true;
-    // thread 0: residual loads issued but not yet waited for (per buffer), so an
+    // lane 0: residual loads issued but not yet waited for (per buffer), so an
     // abort can let them land before the CTA exits
     uint32_t res_out = 0, res_par[2] = {0, 0};
-    auto issue_res = [&](uint32_t g, int col, int m0, int b) {
+    auto issue_res = [&](uint32_t g, int col, int r0, int b) {
       const int rb = g & 1;
-      mbar_arrive_expect_tx(res_full(rb), kEpiTile);
-      tma_load_3d(res_st + rb * kEpiTile, &tm_res, col, m0, b, res_full(rb));
+      mbar_arrive_expect_tx(res_full(warp, rb), kWTile);
+      tma_load_3d(res_st + rb * kEpiTile + warp * kWTile, &tm_res, col, r0, b, res_full(warp, rb));
       res_out |= 1u << rb;
       res_par[rb] = (g >> 1) & 1;
     };
-    for (int tj = 0; tj < my_tiles && ok; ++tj) {
+    for (int tj = 0; tj < my_tiles; ++tj) {
       int b, mt, nt;
       tile_coords(blockIdx.x + tj * gridDim.x, b, mt, nt);
       const int m0 = mt * kBM;
+      const int r0 = m0 + warp * 32;        // this warp's first row
+      const bool rows_in = r0 < p.M;        // boxes entirely past M are skipped
       const int rem_cols = p.Nc - nt * BN;
       const int ngroups = rem_cols >= BN ? BN / kEG : (rem_cols + kEG - 1) / kEG;
-      // this tile's per-channel scale / shift, staged once in shared memory (the
-      // previous tile's last reads happened before its last group barrier)
+      // all four warps are done with the previous tile (and its staged scale /
+      // shift); an abort in any of them ends the loop for all
+      ok = named_bar_and(ok, kEpiThreads);
+      if (!ok) break;
+      // this tile's per-channel scale / shift, staged once in shared memory
       if (p.scale || p.shift) {
         for (int c = et; c < BN; c += kEpiThreads) {
           const int gc = nt * BN + c;
@@ -504,14 +514,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         named_bar_sync(kEpiThreads);
       }
       // residual blocks of the first two groups (later ones after each use)
-      if (p.res && et == 0) {
-        for (int g = 0; g < 2 && g < ngroups; ++g) issue_res(grp + g, nt * BN + g * kEG, m0, b);
+      if (p.res && lane == 0 && rows_in) {
+        for (int g = 0; g < 2 && g < ngroups; ++g) issue_res(grp + g, nt * BN + g * kEG, r0, b);
       }
       const int nch = L::kPromote ? (p.num_kb + L::kChunkKB - 1) / L::kChunkKB : 1;
       for (int ch = 0; ch < nch; ++ch) {
         const int cb = L::kPromote ? (cc & 1) : (tj & 1);
         const uint32_t cpar = L::kPromote ? ((cc >> 1) & 1) : ((tj >> 1) & 1);
-        ok = named_bar_and(mbar_wait(acc_full(cb), cpar, abort_flag, p.status), kEpiThreads);
+        ok = named_bar_and(ok && mbar_wait(acc_full(cb), cpar, abort_flag, p.status), kEpiThreads);
         if (!ok) break;
         tc_fence_after();
         const bool last = ch == nch - 1;
@@ -597,9 +607,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           bool w = true;
-          if (p.res) {
-            w = mbar_wait(res_full(buf), (grp >> 1) & 1, abort_flag, p.status);
-            if (w && et == 0) res_out &= ~(1u << buf);
+          if (p.res && rows_in) {
+            w = mbar_wait(res_full(warp, buf), (grp >> 1) & 1, abort_flag, p.status);
+            if (w && lane == 0) res_out &= ~(1u << buf);
 #pragma unroll
             for (int q4 = 0; q4 < kEG / 4; ++q4) {
               const float4 rv = ld_shared_f4(res_st + buf * kEpiTile + swz_eg<kEG>(et, q4));
@@ -610,36 +620,38 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int e = 0; e < kEG; ++e) v[e] = v[e] > 0.f ? v[e] : 0.f;
           }
-          // the staging tile of two groups ago must have been read by its TMA store
-          if (et == 0) bulk_wait_group_read<1>();
-          ok = named_bar_and(w, kEpiThreads);
-          if (!ok) break;
+          // this warp's staging rows of two groups ago must have been read by its
+          // TMA store (the warp vote below also orders lane 0's wait first)
+          if (lane == 0) bulk_wait_group_read<1>();
+          if (!__all_sync(0xffffffffu, w)) {
+            ok = false;  // decided with the other warps at the next barrier
+            break;
+          }
           const uint32_t ost = out_st + buf * kEpiTile;
 #pragma unroll
           for (int q4 = 0; q4 < kEG / 4; ++q4)
             sts_v4(ost + swz_eg<kEG>(et, q4), v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
           fence_proxy_async_smem();
-          named_bar_sync(kEpiThreads);
-          if (et == 0) {
-            tma_store_3d(&tm_y, col0, m0, b, ost);
+          __syncwarp();
+          if (lane == 0 && rows_in) {
+            tma_store_3d(&tm_y, col0, r0, b, ost + warp * kWTile);
             bulk_commit_group();
-            if (p.res && j + 2 < ngroups) issue_res(grp + 2, col0 + 2 * kEG, m0, b);  // freed buffer
+            if (p.res && j + 2 < ngroups) issue_res(grp + 2, col0 + 2 * kEG, r0, b);  // freed buffer
           }
           ++grp;
         }
-        if (!ok) break;
         if (!last) tmem_st_wait();
         tc_fence_before();
         mbar_arrive(acc_empty(cb));
         if (L::kPromote) ++cc;
       }
     }
-    if (et == 0) {
+    if (lane == 0) {
       bulk_wait_group<0>();  // stores complete before the CTA exits
       for (int rb = 0; rb < 2; ++rb)
         if (res_out & (1u << rb)) {  // only after an abort
           volatile int no_abort = 0;
-          mbar_wait(res_full(rb), res_par[rb], &no_abort, p.status);
+          mbar_wait(res_full(warp, rb), res_par[rb], &no_abort, p.status);
         }
     }
   }
@@ -671,7 +683,8 @@ EncodeTiledFn3 tiled_fn() {
 }
 
 // [batches][rows][cols] fp32 output / residual with row stride ld, batch stride
-// bstride (elements); 128 x eg boxes (eg = 16 or 32 columns, 64- or 128-byte swizzle).
+// bstride (elements); 32-row x eg boxes (one per epilogue warp; eg = 16 or 32
+// columns, 64- or 128-byte swizzle).
 int encode_out_map(const float* base, int cols, int rows, int batches, int ld, long long bstride,
                    int eg, CUtensorMap* map) {
   EncodeTiledFn3 fn = tiled_fn();
@@ -679,7 +692,7 @@ int encode_out_map(const float* base, int cols, int rows, int batches, int ld, l
   const long long bs = batches > 1 ? bstride : (long long)rows * ld;
   cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)batches};
   cuuint64_t strides[2] = {(cuuint64_t)ld * 4, (cuuint64_t)bs * 4};
-  cuuint32_t box[3] = {(cuuint32_t)eg, (cuuint32_t)kBM, 1u};
+  cuuint32_t box[3] = {(cuuint32_t)eg, 32u, 1u};
   cuuint32_t es[3] = {1u, 1u, 1u};
   return (int)fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box,
                  es, CU_TENSOR_MAP_INTERLEAVE_NONE,
