@@ -189,8 +189,11 @@ int conv_plan_init(onnxb200_handle* h, const onnxb200_conv_desc* din, int cs_in,
   const int CO = (int)d.c_out;
   size_t need = 0;
   size_t off_hi = 0, off_lo = 0, off_scale = 0, off_shift = 0, off_w = 0;
+  p->pairs = p->use_tc && p->prec != kPrecBF16 && cs_in == 4 && d.stride_w == 2 && d.dil_w == 1 &&
+             d.w % 2 == 0 && d.kw > 1;
+  const int kwp = (int)((d.kw + (d.pad_left & 1) + 1) / 2);  // pair taps
   if (p->use_tc) {
-    p->K = (int)(d.kh * d.kw * cs_in);
+    p->K = p->pairs ? (int)(d.kh * kwp * 8) : (int)(d.kh * d.kw * cs_in);
     p->kpad = igemm_kpad(p->K, p->prec);
     p->num_kb = p->kpad / igemm_block_k(p->prec);
     const size_t esz = p->prec == kPrecBF16 ? 2 : 4;
@@ -238,7 +241,8 @@ int conv_plan_init(onnxb200_handle* h, const onnxb200_conv_desc* din, int cs_in,
     if (p->prec == kPrec3xTF32) p->w_lo = basep + off_lo;
     // OIHW element (co, ci, r, s) -> k = (r*KW + s)*cs_in + ci
     rc = pack_b_launch(w, CO, p->K, p->kpad, cs_in, (int)d.c, CO, 0, d.c * d.kh * d.kw, 1,
-                       d.kh * d.kw, p->prec, p->w_hi, p->w_lo, st);
+                       d.kh * d.kw, p->prec, p->w_hi, p->w_lo, st, p->pairs ? (int)d.kw : 0,
+                       (int)(d.pad_left & 1));
     h->launches++;
     if (rc) return cuda_check(h, (cudaError_t)rc, "weight packing");
     IgemmParams q{};
@@ -310,10 +314,17 @@ int conv_plan_exec_nhwc(onnxb200_handle* h, const onnxb200_conv_plan* p, const f
     q.status = h->d_status;
     q.m_tiles = (q.M + 127) / 128;
     q.n_tiles = (q.Nc + p->bn - 1) / p->bn;
+    if (p->pairs) {  // the same NHWC memory as [N][H][W/2][8], stride 1 over pair taps
+      q.Win = (int)(d.w / 2);
+      q.Cs = 8;
+      q.KW = (int)((d.kw + (d.pad_left & 1) + 1) / 2);
+      q.sw = 1;
+      q.pw = (int)((d.pad_left + 1) / 2);
+    }
     q.a_mode = pick_a_mode(q, p->prec);
     CUtensorMap am{};
     if (q.a_mode != kALoadGather) {
-      const int rows = q.a_mode == kALoadTma2d ? (int)(d.n * d.h * d.w) : (int)d.n;
+      const int rows = q.a_mode == kALoadTma2d ? (int)d.n * q.Hin * q.Win : (int)d.n;
       const int er = encode_a_map(q, rows, &am);
       if (er) return set_error(h, ONNXB200_ERR_EXECUTION, "Conv: A tensor map encode failed: " + std::to_string(er));
     }

@@ -41,6 +41,10 @@ struct onnxb200_conv_plan {
   float* shift = nullptr;    // epilogue per-channel addend (bias / BN) or null
   CUtensorMap tm_hi{}, tm_lo{};
   int64_t weight_bytes = 0;
+  // Pixel pairs (4-channel input, horizontal stride 2, even width): the NHWC
+  // input is read as [N][H][W/2][8] and the convolution runs with stride 1 over
+  // ceil((KW + pw%2)/2) pair taps -- the same memory, half the TMA box rows.
+  bool pairs = false;
 };
 
 namespace ob2 {

@@ -96,9 +96,14 @@ int gemm_simt_launch(const float* a, const float* b, int batches, const long lon
 //   src[(row/rpg)*gs + (row%rpg)*rs + (k/Cs)*ts + (k%Cs)*cs]
 // for k%Cs < Creal, zero otherwise (and zero for k >= K).  For 3xTF32 both hi
 // and lo are written; for TF32 only hi; for BF16 `hi` receives bf16 values.
+//
+// pair_kw > 0 selects the pixel-pair layout of a stride-2 convolution over a
+// Cs-channel input read as 2*Cs-channel pixel pairs: k = (r*KWp + q')*2Cs + h*Cs + c
+// holds original tap (r, q = 2q' + h - pair_odd) (zero if q is outside [0, pair_kw)),
+// with KWp = (pair_kw + pair_odd + 1) / 2; Cs is then the original channel stride.
 int pack_b_launch(const float* src, int rows, int K, int Kpad, int Cs, int Creal, int rpg,
                   long long gs, long long rs, long long ts, long long cs, int precision,
-                  void* hi, void* lo, cudaStream_t stream);
+                  void* hi, void* lo, cudaStream_t stream, int pair_kw = 0, int pair_odd = 0);
 
 // NCHW -> NHWC with channel padding to Cp (zero-filled), and NHWC -> NCHW.
 int nchw_to_nhwc_launch(const float* x, int N, int C, int H, int W, int Cp, float* y,

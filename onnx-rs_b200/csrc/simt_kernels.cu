@@ -155,7 +155,7 @@ int gemm_simt_launch(const float* a, const float* b, int batches, const long lon
 // ------------------------------------------------------------------ weight packing
 __global__ void pack_b_kernel(const float* __restrict__ src, int rows, int K, int Kpad, int Cs,
                               int Creal, int rpg, long long gs, long long rs, long long ts,
-                              long long cs, int prec, void* hi, void* lo) {
+                              long long cs, int prec, void* hi, void* lo, int pair_kw, int pair_odd) {
   const long long total = (long long)rows * Kpad;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
@@ -163,8 +163,16 @@ __global__ void pack_b_kernel(const float* __restrict__ src, int rows, int K, in
     const int k = (int)(i % Kpad);
     float v = 0.f;
     if (k < K) {
-      const int tap = k / Cs, c = k % Cs;
-      if (c < Creal) v = src[(long long)(row / rpg) * gs + (long long)(row % rpg) * rs + tap * ts + c * cs];
+      int tap = k / Cs, c = k % Cs;
+      if (pair_kw) {  // pixel pairs: k = (r*KWp + q')*2Cs + h*Cs + c
+        const int kwp = (pair_kw + pair_odd + 1) / 2;
+        const int tp = k / (2 * Cs), c8 = k - tp * 2 * Cs;
+        const int r = tp / kwp, q = 2 * (tp - r * kwp) + c8 / Cs - pair_odd;
+        c = c8 % Cs;
+        tap = (q >= 0 && q < pair_kw) ? r * pair_kw + q : -1;
+      }
+      if (tap >= 0 && c < Creal)
+        v = src[(long long)(row / rpg) * gs + (long long)(row % rpg) * rs + tap * ts + c * cs];
     }
     if (prec == kPrecBF16) {
       reinterpret_cast<__nv_bfloat16*>(hi)[i] = __float2bfloat16_rn(v);
@@ -185,11 +193,12 @@ __global__ void pack_b_kernel(const float* __restrict__ src, int rows, int K, in
 
 int pack_b_launch(const float* src, int rows, int K, int Kpad, int Cs, int Creal, int rpg,
                   long long gs, long long rs, long long ts, long long cs, int prec, void* hi,
-                  void* lo, cudaStream_t st) {
+                  void* lo, cudaStream_t st, int pair_kw, int pair_odd) {
   const long long total = (long long)rows * Kpad;
   if (total == 0) return 0;
   pack_b_kernel<<<grid_for(total, kBlock), kBlock, 0, st>>>(src, rows, K, Kpad, Cs, Creal, rpg,
-                                                            gs, rs, ts, cs, prec, hi, lo);
+                                                            gs, rs, ts, cs, prec, hi, lo, pair_kw,
+                                                            pair_odd);
   return (int)cudaGetLastError();
 }
 

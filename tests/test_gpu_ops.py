@@ -53,6 +53,8 @@ SMALL = [
     ("c5_odd_channels", (2, 5, 9, 9), 12, 3, 1, 1, 1, 1),
     ("c3_dil2_s2", (2, 3, 17, 19), 16, 3, 2, 2, 2, 1),
     ("c6_5x5_s2", (1, 6, 21, 18), 24, 5, 2, 2, 1, 1),
+    ("c3_7x7_s2_even_w", (2, 3, 30, 28), 24, 7, 2, 3, 1, 1),
+    ("c4_3x3_s2_p2_even_w", (1, 4, 18, 20), 16, 3, 2, 2, 1, 1),
 ]
 
 
