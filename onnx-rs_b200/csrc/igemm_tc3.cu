@@ -58,14 +58,14 @@ constexpr int kSmemBudget = 224 * 1024;
 // EG = 16 halves the staging memory so that 3xTF32 with BN = 128 fits four 48 KB
 // operand stages, which pays when the tile's K loop is long.
 
-template <int PREC, int BN, int EG>
+template <int PREC, int BN, int EG, int NB>
 struct Layout {
   static constexpr int kEpiTile = kBM * EG * 4;
   static constexpr bool kSplit = (PREC == kPrec3xTF32);
   static constexpr int kARaw = kBM * kBK * 4;   // 16 KB
   static constexpr int kBBytes = BN * kBK * 4;  // one B operand (hi or lo)
   static constexpr int kStage = kARaw + (kSplit ? 2 : 1) * kBBytes;
-  static constexpr int kEpiBytes = 4 * kEpiTile;  // out[2] + res[2]
+  static constexpr int kEpiBytes = 2 * NB * kEpiTile;  // out[NB] + res[NB]
   static constexpr int kS1raw = (kSmemBudget - kEpiBytes) / kStage;
   static constexpr int kS1cap = kS1raw > 8 ? 8 : kS1raw;
   static constexpr bool kPromote = kSplit;
@@ -89,19 +89,19 @@ struct Layout {
   static constexpr int kS1 = kS1cap;
   static constexpr int kS2 = (kSplit && kS2raw < kS1) ? kS2raw : kS1;
   static_assert(kS2 >= 2, "TMEM too small for two A slots");
-  static_assert(kS1 >= 3, "shared memory too small");
+  static_assert(kS1 >= 2, "shared memory too small");
   static constexpr int kACol0 = kAccCols;
   static constexpr int kTmemCols = 512;
-  static constexpr int kOffOut = 0;                     // out[2]  (1024-aligned tiles)
-  static constexpr int kOffRes = 2 * kEpiTile;          // res[2]
-  static constexpr int kOffA = 4 * kEpiTile;            // raw A stages
+  static constexpr int kOffOut = 0;                     // out[NB]  (1024-aligned tiles)
+  static constexpr int kOffRes = NB * kEpiTile;         // res[NB]
+  static constexpr int kOffA = 2 * NB * kEpiTile;       // raw A stages
   static constexpr int kOffB = kOffA + kS1 * kARaw;     // B hi stages
   static constexpr int kBStride = (kStack ? 2 : 1) * kBBytes;  // stage s at kOffB + s * kBStride
   static constexpr int kOffBlo = kStack ? kOffB + kBBytes : kOffB + kS1 * kBBytes;  // B lo stages
   static constexpr int kOffBar = kOffB + kS1 * kBBytes + (kSplit ? kS1 * kBBytes : 0);
   // s1_full[S1], s1_empty[S1], t_full[S2], acc_full[2], acc_empty[2],
   // res_full[4 warps][2], drain
-  static constexpr int kNumBars = 2 * kS1 + kS2 + 13;
+  static constexpr int kNumBars = 2 * kS1 + kS2 + 4 * NB + 7;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kOffSS = (kOffMisc + 16 + 127) / 128 * 128;  // scale[BN], shift[BN]
   static_assert(kOffSS % 16 == 0, "float4 reads of the staged scale / shift");
@@ -126,12 +126,12 @@ __device__ __forceinline__ void sts_v4(uint32_t addr, float a, float b, float c,
                : "memory");
 }
 
-template <int PREC, int BN, int EG>
+template <int PREC, int BN, int EG, int NB>
 __global__ void __launch_bounds__(kThreads, 1)
     igemm_tc3_kernel(const __grid_constant__ IgemmParams p, const __grid_constant__ CUtensorMap tm_hi,
                      const __grid_constant__ CUtensorMap tm_lo, const __grid_constant__ CUtensorMap tm_a,
                      const __grid_constant__ CUtensorMap tm_y, const __grid_constant__ CUtensorMap tm_res) {
-  using L = Layout<PREC, BN, EG>;
+  using L = Layout<PREC, BN, EG, NB>;
   constexpr int kEG = EG;
   constexpr int kEpiTile = L::kEpiTile;
   constexpr int S1 = L::kS1;
@@ -149,8 +149,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto t_full = [&](int a) { return bar0 + 8u * (2 * S1 + a); };
   auto acc_full = [&](int b) { return bar0 + 8u * (2 * S1 + S2 + b); };
   auto acc_empty = [&](int b) { return bar0 + 8u * (2 * S1 + S2 + 2 + b); };
-  auto res_full = [&](int w, int b) { return bar0 + 8u * (2 * S1 + S2 + 4 + 2 * w + b); };
-  const uint32_t drain_bar = bar0 + 8u * (2 * S1 + S2 + 12);
+  auto res_full = [&](int w, int b) { return bar0 + 8u * (2 * S1 + S2 + 4 + NB * w + b); };
+  const uint32_t drain_bar = bar0 + 8u * (2 * S1 + S2 + 4 + 4 * NB);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + L::kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + L::kOffMisc + 4);
   float* ss_scale = reinterpret_cast<float*>(gbase + L::kOffSS);
@@ -170,8 +170,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int b = 0; b < 2; ++b) {
       mbar_init(acc_full(b), 1);
       mbar_init(acc_empty(b), kEpiThreads);
-      for (int w = 0; w < 4; ++w) mbar_init(res_full(w, b), 1);
     }
+    for (int w = 0; w < 4; ++w)
+      for (int b = 0; b < NB; ++b) mbar_init(res_full(w, b), 1);
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
     fence_mbarrier_init();
@@ -480,17 +481,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_addr = (uint32_t)(warp * 32) << 16;
     constexpr int kWTile = kEpiTile / 4;  // this warp's 32 rows of a staging tile
     uint32_t cc = 0;   // accumulator chunks consumed
-    uint32_t grp = 0;  // kEG-column output groups produced (staging buffer = grp & 1)
+    uint32_t grp = 0;  // kEG-column output groups produced (staging buffer = grp % NB)
     bool ok = true;
     // lane 0: residual loads issued but not yet waited for (per buffer), so an
     // abort can let them land before the CTA exits
-    uint32_t res_out = 0, res_par[2] = {0, 0};
+    uint32_t res_out = 0, res_par[NB] = {};
     auto issue_res = [&](uint32_t g, int col, int r0, int b) {
-      const int rb = g & 1;
+      const int rb = g % NB;
       mbar_arrive_expect_tx(res_full(warp, rb), kWTile);
       tma_load_3d(res_st + rb * kEpiTile + warp * kWTile, &tm_res, col, r0, b, res_full(warp, rb));
       res_out |= 1u << rb;
-      res_par[rb] = (g >> 1) & 1;
+      res_par[rb] = (g / NB) & 1;
     };
     for (int tj = 0; tj < my_tiles; ++tj) {
       int b, mt, nt;
@@ -513,9 +514,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         named_bar_sync(kEpiThreads);
       }
-      // residual blocks of the first two groups (later ones after each use)
+      // residual blocks of the first NB groups (later ones after each use)
       if (p.res && lane == 0 && rows_in) {
-        for (int g = 0; g < 2 && g < ngroups; ++g) issue_res(grp + g, nt * BN + g * kEG, r0, b);
+        for (int g = 0; g < NB && g < ngroups; ++g) issue_res(grp + g, nt * BN + g * kEG, r0, b);
       }
       const int nch = L::kPromote ? (p.num_kb + L::kChunkKB - 1) / L::kChunkKB : 1;
       for (int ch = 0; ch < nch; ++ch) {
@@ -590,7 +591,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           // ---- final values of this group
           const int col0 = nt * BN + j * kEG;
-          const int buf = grp & 1;
+          const int buf = grp % NB;
           float v[kEG];
 #pragma unroll
           for (int e = 0; e < kEG; ++e) v[e] = __uint_as_float(r[e]);
@@ -608,7 +609,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           bool w = true;
           if (p.res && rows_in) {
-            w = mbar_wait(res_full(warp, buf), (grp >> 1) & 1, abort_flag, p.status);
+            w = mbar_wait(res_full(warp, buf), (grp / NB) & 1, abort_flag, p.status);
             if (w && lane == 0) res_out &= ~(1u << buf);
 #pragma unroll
             for (int q4 = 0; q4 < kEG / 4; ++q4) {
@@ -620,9 +621,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int e = 0; e < kEG; ++e) v[e] = v[e] > 0.f ? v[e] : 0.f;
           }
-          // this warp's staging rows of two groups ago must have been read by its
+          // this warp's staging rows of NB groups ago must have been read by its
           // TMA store (the warp vote below also orders lane 0's wait first)
-          if (lane == 0) bulk_wait_group_read<1>();
+          if (lane == 0) bulk_wait_group_read<NB - 1>();
           if (!__all_sync(0xffffffffu, w)) {
             ok = false;  // decided with the other warps at the next barrier
             break;
@@ -636,7 +637,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lane == 0 && rows_in) {
             tma_store_3d(&tm_y, col0, r0, b, ost + warp * kWTile);
             bulk_commit_group();
-            if (p.res && j + 2 < ngroups) issue_res(grp + 2, col0 + 2 * kEG, r0, b);  // freed buffer
+            if (p.res && j + NB < ngroups) issue_res(grp + NB, col0 + NB * kEG, r0, b);  // freed buffer
           }
           ++grp;
         }
@@ -648,7 +649,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (lane == 0) {
       bulk_wait_group<0>();  // stores complete before the CTA exits
-      for (int rb = 0; rb < 2; ++rb)
+      for (int rb = 0; rb < NB; ++rb)
         if (res_out & (1u << rb)) {  // only after an abort
           volatile int no_abort = 0;
           mbar_wait(res_full(warp, rb), res_par[rb], &no_abort, p.status);
@@ -700,13 +701,13 @@ int encode_out_map(const float* base, int cols, int rows, int batches, int ld, l
                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
 
-template <int PREC, int BN, int EG>
+template <int PREC, int BN, int EG, int NB>
 int launch3_t(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap& lo,
               const CUtensorMap& am, int num_sms, cudaStream_t st) {
-  using L = Layout<PREC, BN, EG>;
+  using L = Layout<PREC, BN, EG, NB>;
   static bool attr_set = false;
   if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(igemm_tc3_kernel<PREC, BN, EG>,
+    cudaError_t e = cudaFuncSetAttribute(igemm_tc3_kernel<PREC, BN, EG, NB>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
     if (e != cudaSuccess) return (int)e;
     attr_set = true;
@@ -721,25 +722,36 @@ int launch3_t(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap& lo
   const int total = p.m_tiles * p.n_tiles * p.batches;
   const int grid = total < num_sms ? total : num_sms;
   if (grid <= 0) return 0;
-  igemm_tc3_kernel<PREC, BN, EG><<<grid, kThreads, L::kBytes, st>>>(p, hi, lo, am, ym, rm);
+  igemm_tc3_kernel<PREC, BN, EG, NB><<<grid, kThreads, L::kBytes, st>>>(p, hi, lo, am, ym, rm);
   return (int)cudaGetLastError();
 }
 
 }  // namespace
 
 constexpr int kLongK = 16;  // k-blocks (K >= 512)
+constexpr int kShortK = 2;  // k-blocks (K <= 64)
 
 int igemm3_launch(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap& lo,
                   const CUtensorMap& am, int precision, int bn, int num_sms, cudaStream_t st) {
   // 3xTF32, BN = 128: 16-column epilogue groups buy a fourth operand stage,
   // worth it once the K loop of a tile is long (short-K layers are bound by
   // their epilogue, which 32-column groups store faster)
-  if (precision == kPrec3xTF32 && bn == 64) return launch3_t<kPrec3xTF32, 64, 32>(p, hi, lo, am, num_sms, st);
+  // Short K loops are bound by the epilogue's HBM traffic: four staging
+  // buffers (more stores and residual loads in flight) instead of operand stages.
+  const bool short_k = p.num_kb <= kShortK;
+  if (precision == kPrec3xTF32 && bn == 64)
+    return short_k ? launch3_t<kPrec3xTF32, 64, 32, 4>(p, hi, lo, am, num_sms, st)
+                   : launch3_t<kPrec3xTF32, 64, 32, 2>(p, hi, lo, am, num_sms, st);
   if (precision == kPrec3xTF32 && bn == 128)
-    return p.num_kb >= kLongK ? launch3_t<kPrec3xTF32, 128, 16>(p, hi, lo, am, num_sms, st)
-                              : launch3_t<kPrec3xTF32, 128, 32>(p, hi, lo, am, num_sms, st);
-  if (precision == kPrecTF32 && bn == 64) return launch3_t<kPrecTF32, 64, 32>(p, hi, lo, am, num_sms, st);
-  if (precision == kPrecTF32 && bn == 128) return launch3_t<kPrecTF32, 128, 32>(p, hi, lo, am, num_sms, st);
+    return p.num_kb >= kLongK ? launch3_t<kPrec3xTF32, 128, 16, 2>(p, hi, lo, am, num_sms, st)
+           : short_k          ? launch3_t<kPrec3xTF32, 128, 32, 4>(p, hi, lo, am, num_sms, st)
+                              : launch3_t<kPrec3xTF32, 128, 32, 2>(p, hi, lo, am, num_sms, st);
+  if (precision == kPrecTF32 && bn == 64)
+    return short_k ? launch3_t<kPrecTF32, 64, 32, 4>(p, hi, lo, am, num_sms, st)
+                   : launch3_t<kPrecTF32, 64, 32, 2>(p, hi, lo, am, num_sms, st);
+  if (precision == kPrecTF32 && bn == 128)
+    return short_k ? launch3_t<kPrecTF32, 128, 32, 4>(p, hi, lo, am, num_sms, st)
+                   : launch3_t<kPrecTF32, 128, 32, 2>(p, hi, lo, am, num_sms, st);
   return (int)cudaErrorInvalidValue;
 }
 
