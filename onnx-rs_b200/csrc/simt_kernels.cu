@@ -68,12 +68,130 @@ __global__ void conv_direct_kernel(const float* __restrict__ x, int N, int H, in
   }
 }
 
+// Grouped convolution with 4-aligned group widths (e.g. ResNeXt's 32 groups of
+// 4 channels): one thread per (output pixel, 4 output channels of one group),
+// 16-byte input and output vectors, the OIHW weights staged in shared memory as
+// [tap][ci][co] (the lanes of a warp hold consecutive output-channel quadruples
+// of one pixel and read one 16-byte weight vector each).  KH, KW, CG4 = cg / 4
+// are compile-time (0 = runtime) so that a 3x3 filter's loads are all issued
+// before its FMAs.  Sums over (kh, kw, ci) in fp32.
+template <int KH_, int KW_, int CG4_>
+__global__ void conv_grouped_v4_kernel(const float* __restrict__ x, int H, int W, int Cs,
+                                       const float* __restrict__ w, int CO, int cg_rt, int cog,
+                                       int KH_rt, int KW_rt, int sh, int sw, int ph, int pw, int dh,
+                                       int dw, int OH, int OW, long long total4,
+                                       const float* __restrict__ scale,
+                                       const float* __restrict__ shift, const float* __restrict__ res,
+                                       int relu, float* __restrict__ y) {
+  const int KH = KH_ ? KH_ : KH_rt, KW = KW_ ? KW_ : KW_rt, cg = CG4_ ? 4 * CG4_ : cg_rt;
+  extern __shared__ float ws[];
+  const int wn = CO * cg * KH * KW;
+  for (int i = threadIdx.x; i < wn; i += blockDim.x) {  // i = (tap*cg + ci)*CO + co
+    const int co = i % CO, tc = i / CO;
+    const int ci = tc % cg, tap = tc / cg;
+    ws[i] = __ldg(w + ((long long)co * cg + ci) * (KH * KW) + tap);
+  }
+  __syncthreads();
+  const unsigned CO4 = CO / 4;
+  // 32-bit index math (the launcher guarantees total4 < 2^31): 64-bit divisions
+  // would dominate the cost of this kernel
+  for (unsigned idx = blockIdx.x * blockDim.x + threadIdx.x; idx < (unsigned)total4;
+       idx += gridDim.x * blockDim.x) {
+    const int co0 = (int)(idx % CO4) * 4;
+    const unsigned pix = idx / CO4;
+    const int ow = (int)(pix % (unsigned)OW);
+    const unsigned t = pix / (unsigned)OW;
+    const int oh = (int)(t % (unsigned)OH);
+    const long long n = t / (unsigned)OH;
+    const int cin0 = (co0 / cog) * cg;
+    const float* xb = x + n * H * W * Cs + cin0;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    if constexpr (KH_ > 0 && KW_ > 0 && CG4_ > 0) {
+      float4 xin[KH_ * KW_][CG4_];
+#pragma unroll
+      for (int r = 0; r < KH_; ++r)
+#pragma unroll
+        for (int q = 0; q < KW_; ++q) {
+          const int ih = oh * sh - ph + r * dh, iw = ow * sw - pw + q * dw;
+          const bool in = (unsigned)ih < (unsigned)H && (unsigned)iw < (unsigned)W;
+          const float4* xp = reinterpret_cast<const float4*>(xb + ((long long)ih * W + iw) * Cs);
+#pragma unroll
+          for (int c4 = 0; c4 < CG4_; ++c4)
+            xin[r * KW_ + q][c4] = in ? __ldg(xp + c4) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+      for (int tap = 0; tap < KH_ * KW_; ++tap)
+#pragma unroll
+        for (int c4 = 0; c4 < CG4_; ++c4) {
+          const float xs[4] = {xin[tap][c4].x, xin[tap][c4].y, xin[tap][c4].z, xin[tap][c4].w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float4 wv = *reinterpret_cast<const float4*>(ws + (tap * cg + 4 * c4 + e) * CO + co0);
+            acc[0] = fmaf(xs[e], wv.x, acc[0]);
+            acc[1] = fmaf(xs[e], wv.y, acc[1]);
+            acc[2] = fmaf(xs[e], wv.z, acc[2]);
+            acc[3] = fmaf(xs[e], wv.w, acc[3]);
+          }
+        }
+    } else {
+      for (int r = 0; r < KH; ++r) {
+        const int ih = oh * sh - ph + r * dh;
+        if ((unsigned)ih >= (unsigned)H) continue;
+        for (int q = 0; q < KW; ++q) {
+          const int iw = ow * sw - pw + q * dw;
+          if ((unsigned)iw >= (unsigned)W) continue;
+          const float4* xp = reinterpret_cast<const float4*>(xb + ((long long)ih * W + iw) * Cs);
+          const float* wt = ws + (r * KW + q) * cg * CO + co0;
+          for (int c4 = 0; c4 < cg / 4; ++c4) {
+            const float4 xv = __ldg(xp + c4);
+            const float xs[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float4 wv = *reinterpret_cast<const float4*>(wt + (4 * c4 + e) * CO);
+              acc[0] = fmaf(xs[e], wv.x, acc[0]);
+              acc[1] = fmaf(xs[e], wv.y, acc[1]);
+              acc[2] = fmaf(xs[e], wv.z, acc[2]);
+              acc[3] = fmaf(xs[e], wv.w, acc[3]);
+            }
+          }
+        }
+      }
+    }
+    const long long o = (long long)pix * CO + co0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float v = epi(acc[j], scale, shift, co0 + j);
+      if (res) v += res[o + j];
+      if (relu) v = v > 0.f ? v : 0.f;
+      acc[j] = v;
+    }
+    *reinterpret_cast<float4*>(y + o) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+  }
+}
+
 int conv_direct_launch(const float* x, int N, int H, int W, int C, int Cs, const float* w, int CO,
                        int KH, int KW, int sh, int sw, int ph, int pw, int dh, int dw, int group, int OH,
                        int OW, const float* scale, const float* shift, const float* res, int relu,
                        float* y, cudaStream_t st) {
   const long long total = (long long)N * OH * OW * CO;
   if (total == 0) return 0;
+  const int cg = C / group, cog = CO / group;
+  const size_t wbytes = (size_t)CO * cg * KH * KW * sizeof(float);
+  auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+  if (group > 1 && cg % 4 == 0 && cog % 4 == 0 && Cs % 4 == 0 && wbytes <= 96 * 1024 && a16(x) &&
+      a16(y) && (!res || a16(res)) && total / 4 < (1ll << 31)) {
+    const long long total4 = total / 4;
+    const int blocks = (int)std::min<long long>((total4 + 255) / 256, 148LL * 4);
+    auto go = [&](auto kern) {
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+      kern<<<blocks, 256, wbytes, st>>>(x, H, W, Cs, w, CO, cg, cog, KH, KW, sh, sw, ph, pw, dh, dw,
+                                        OH, OW, total4, scale, shift, res, relu, y);
+    };
+    if (KH == 3 && KW == 3 && cg == 4) go(conv_grouped_v4_kernel<3, 3, 1>);
+    else if (KH == 3 && KW == 3 && cg == 8) go(conv_grouped_v4_kernel<3, 3, 2>);
+    else go(conv_grouped_v4_kernel<0, 0, 0>);
+    return (int)cudaGetLastError();
+  }
   conv_direct_kernel<<<grid_for(total, kBlock), kBlock, 0, st>>>(
       x, N, H, W, C, Cs, w, CO, KH, KW, sh, sw, ph, pw, dh, dw, group, OH, OW, scale, shift, res,
       relu, y);

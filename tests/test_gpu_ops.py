@@ -50,6 +50,8 @@ SMALL = [
     ("c128_1x1_wide", (2, 128, 8, 8), 256, 1, 1, 0, 1, 1),
     ("c8_co20", (1, 8, 9, 9), 20, 3, 1, 1, 1, 1),
     ("grouped", (2, 32, 10, 10), 32, 3, 1, 1, 1, 8),
+    ("grouped_cg8_s2", (2, 32, 9, 11), 16, 3, 2, 1, 1, 4),
+    ("grouped_cg3", (1, 12, 8, 8), 12, 3, 1, 1, 1, 4),
     ("c5_odd_channels", (2, 5, 9, 9), 12, 3, 1, 1, 1, 1),
     ("c3_dil2_s2", (2, 3, 17, 19), 16, 3, 2, 2, 2, 1),
     ("c6_5x5_s2", (1, 6, 21, 18), 24, 5, 2, 2, 1, 1),
