@@ -520,8 +520,9 @@ int launch_t(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap& lo,
 int igemm_pick_bn(const IgemmParams& p, int precision, int num_sms) {
   const int nc = p.Nc;
   if (nc <= 64) return 64;
-  // tf32 modes: accumulators plus TMEM A stages must fit the 512 TMEM columns
-  if (precision == kPrec3xTF32 || precision == kPrecTF32) return 128;
+  // 3xTF32: the chunked accumulators (3 x BN) plus TMEM A slots must fit the
+  // 512 TMEM columns; TF32 keeps only two whole-tile accumulators
+  if (precision == kPrec3xTF32) return 128;
   const long long mt = (long long)((p.M + kBM - 1) / kBM) * p.batches;
   // Wide tiles halve A re-reads; use them when there are enough tiles to fill the GPU.
   if (nc >= 256 && mt * ((nc + 255) / 256) >= 2ll * num_sms) return 256;

@@ -752,6 +752,7 @@ int igemm3_launch(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap
   if (precision == kPrecTF32 && bn == 128)
     return short_k ? launch3_t<kPrecTF32, 128, 32, 4>(p, hi, lo, am, num_sms, st)
                    : launch3_t<kPrecTF32, 128, 32, 2>(p, hi, lo, am, num_sms, st);
+  if (precision == kPrecTF32 && bn == 256) return launch3_t<kPrecTF32, 256, 32, 2>(p, hi, lo, am, num_sms, st);
   return (int)cudaErrorInvalidValue;
 }
 
