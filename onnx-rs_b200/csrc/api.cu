@@ -189,7 +189,7 @@ int conv_plan_init(onnxb200_handle* h, const onnxb200_conv_desc* din, int cs_in,
   const int CO = (int)d.c_out;
   size_t need = 0;
   size_t off_hi = 0, off_lo = 0, off_scale = 0, off_shift = 0, off_w = 0;
-  p->pairs = p->use_tc && p->prec != kPrecBF16 && cs_in == 4 && d.stride_w == 2 && d.dil_w == 1 &&
+  p->pairs = p->use_tc && cs_in == 4 && d.stride_w == 2 && d.dil_w == 1 &&
              d.w % 2 == 0 && d.kw > 1;
   const int kwp = (int)((d.kw + (d.pad_left & 1) + 1) / 2);  // pair taps
   if (p->use_tc) {

@@ -1,5 +1,5 @@
-// tcgen05 implicit-GEMM kernel for the fp32-input modes (3xTF32 and TF32):
-// convolution without an im2col buffer, and batched broadcast GEMM.
+// tcgen05 implicit-GEMM kernel (3xTF32, TF32 and BF16 modes; fp32 activations
+// and outputs): convolution without an im2col buffer, and batched broadcast GEMM.
 //
 // Replaces the reference's compute_conv2d_im2col + im2col_2d
 // (src/ops/nn/conv.rs:1142-1368), the direct 1x1 path (conv.rs:849-935),
@@ -7,11 +7,13 @@
 // compute_gemm (src/ops/math/gemm.rs:172-291).
 //
 // Persistent, warp-specialised, one 416-thread CTA per SM.  Tile 128 x BN
-// (BN = 64 or 128), k-blocks of 32 fp32 (128-byte swizzled rows).
+// (BN = 64 or 128; 256 in TF32), k-blocks of 32 fp32 (128-byte swizzled rows:
+// TMA moves about one box row per two cycles, so wide rows are fast).
 //   warps 0-3   epilogue: TMEM -> registers, per-channel scale/shift (bias, folded
-//               BatchNormalization), residual, Relu; each 128 x 16 block is staged in
-//               shared memory and written with one TMA store (the hardware clips rows
-//               >= M and columns >= N); residual blocks arrive by TMA load.
+//               BatchNormalization, staged per tile in shared memory), residual,
+//               Relu.  Warp w stores (and loads the residual of) its own 32 rows of
+//               each 16- or 32-column group with its own TMA boxes (the hardware
+//               clips rows >= M and columns >= N).
 //   warps 4-7   A loaders.  TMA modes: one thread issues, per k-block, the A tile
 //               (2-D tile of the [pixels][channels] matrix for 1x1 stride-1 convs and
 //               GEMMs, or an im2col box for k x k convs: the hardware walks 128 output
@@ -19,24 +21,26 @@
 //               tiles.  Taps mode (4, 8 or 16 channels): one im2col box per filter
 //               tap.  Gather mode (other channel counts): 16-byte cp.async copies
 //               with zero fill.
-//   warps 8-11  converters: warp 8+q owns TMEM lanes 32q..32q+31 (= tile rows).  The
-//               MMAs read the raw fp32 A from shared memory as its tf32 hi part (the
-//               tensor core uses the upper 19 bits); in 3xTF32 each thread computes
-//               lo = rna(v - trunc(v)) for its row and writes it to a TMEM A stage.
-//               The stage itself is only rewritten to lay taps-mode boxes out for
-//               the MMA or to zero K padding.
-//   warp 12     TMEM allocation and single-thread tcgen05.mma (kind::tf32; A hi and B
-//               from shared memory, A lo from TMEM).
-// 3xTF32: a*b ~= a_hi*b_hi + a_hi*b_lo + a_lo*b_hi (Ootomo & Yokota, 2022), here with
-// hi = the truncated tf32 and lo = the rounded remainder, for both operands.  The
-// tensor core adds into its fp32 accumulator with truncation, so each TMEM
-// accumulator sums only 4 k-blocks (48 MMAs) and the epilogue warps fold these
-// chunks into a running total with round-to-nearest fp32 adds.
+//   warps 8-11  converters: warp 8+q owns TMEM lanes 32q..32q+31 (= tile rows).
+//               3xTF32: each thread writes hi = trunc_tf32(v) and lo = rna_tf32(v - hi)
+//               of its row to a TMEM A slot; BF16: bf16 pairs; TF32: the MMAs read
+//               the raw fp32 A from shared memory (the tensor core uses its upper 19
+//               bits), which is only rewritten for taps-mode boxes or K padding.
+//   warp 12     TMEM allocation and one thread issuing tcgen05.mma (kind::tf32 or
+//               kind::f16), A from TMEM (from shared memory in TF32), B from shared
+//               memory; this thread's issue rate bounds the kernel.
+// 3xTF32: a*b ~= a_hi*b_hi + a_hi*b_lo + a_lo*b_hi (Ootomo & Yokota, 2022), with the
+// same split for both operands.  With BN = 64 the B hi and lo rows are stacked so
+// that one N = 128 MMA computes two of the three products.  The tensor core adds
+// into its fp32 accumulator with truncation, so each TMEM accumulator sums only 4
+// k-blocks (48 MMAs) and the epilogue warps fold these chunks into a running total
+// with round-to-nearest fp32 adds.
 //
 // Every wait is bounded (kWaitTimeoutNs); on expiry the kernel records
 // ONNXB200_ERR_TIMEOUT in the status word and winds down.  The epilogue warps
-// take every abort decision together (barrier AND-reduction), so none of them is
-// ever left waiting at a named barrier.
+// take every abort decision together (barrier AND-reduction once per chunk and
+// per tile), so none of them is ever left waiting at a named barrier.
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include "kernels.h"
@@ -62,8 +66,10 @@ template <int PREC, int BN, int EG, int NB>
 struct Layout {
   static constexpr int kEpiTile = kBM * EG * 4;
   static constexpr bool kSplit = (PREC == kPrec3xTF32);
+  static constexpr bool kBf16 = (PREC == kPrecBF16);
+  static constexpr bool kTmemA = kSplit || kBf16;  // converters write A to TMEM
   static constexpr int kARaw = kBM * kBK * 4;   // 16 KB
-  static constexpr int kBBytes = BN * kBK * 4;  // one B operand (hi or lo)
+  static constexpr int kBBytes = BN * kBK * (kBf16 ? 2 : 4);  // one B operand (hi or lo)
   static constexpr int kStage = kARaw + (kSplit ? 2 : 1) * kBBytes;
   static constexpr int kEpiBytes = 2 * NB * kEpiTile;  // out[NB] + res[NB]
   static constexpr int kS1raw = (kSmemBudget - kEpiBytes) / kStage;
@@ -84,10 +90,11 @@ struct Layout {
   // A-from-shared-memory MMAs would take.  The TMEM slots form their own ring
   // (S2 <= S1), reused once the commit of the slot's previous item has fired.
   // TF32: A is read from shared memory as it landed; S2 == S1, no TMEM slots.
-  static constexpr int kAStageCols = kSplit ? 2 * kBK : 0;
-  static constexpr int kS2raw = kSplit ? (512 - kAccCols) / kAStageCols : 64;
+  // BF16: A converted to bf16 pairs in TMEM (16 columns per k-block).
+  static constexpr int kAStageCols = kSplit ? 2 * kBK : (kBf16 ? kBK / 2 : 0);
+  static constexpr int kS2raw = kTmemA ? (512 - kAccCols) / kAStageCols : 64;
   static constexpr int kS1 = kS1cap;
-  static constexpr int kS2 = (kSplit && kS2raw < kS1) ? kS2raw : kS1;
+  static constexpr int kS2 = (kTmemA && kS2raw < kS1) ? kS2raw : kS1;
   static_assert(kS2 >= 2, "TMEM too small for two A slots");
   static_assert(kS1 >= 2, "shared memory too small");
   static constexpr int kACol0 = kAccCols;
@@ -111,6 +118,16 @@ struct Layout {
 
 // 64-byte-swizzle layout of a [rows][16 fp32] tile: 16-byte chunk c of row r.
 __device__ __forceinline__ uint32_t swz64(int r, int c) { return r * 64 + ((c ^ ((r >> 1) & 3)) << 4); }
+// K-major operand, 64-byte swizzle (bf16 B tiles): 8-row atoms of 512 bytes.
+__device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(1u) << 16;
+  d |= static_cast<uint64_t>(512u >> 4) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(4u) << 61;  // SWIZZLE_64B
+  return d;
+}
 // 128-byte-swizzle layout of a [rows][32 fp32] tile.
 __device__ __forceinline__ uint32_t swz128(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
 // Staging tile of the epilogue: rows of EG fp32, swizzled like its TMA box.
@@ -348,9 +365,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       // uses the upper 19 bits of the container); the stage is only rewritten
       // when its layout is not the MMA's (taps mode) or padding must be zeroed.
       // 3xTF32: A goes to TMEM, so its shared-memory layout does not matter.
-      const bool rewrite = !L::kSplit && (taps || kvalid < kBK);
+      const bool rewrite = !L::kTmemA && (taps || kvalid < kBK);
       float v[kBK];
-      if (ok && (L::kSplit || rewrite)) {
+      if (ok && (L::kTmemA || rewrite)) {
 #pragma unroll
         for (int c = 0; c < kBK / 4; ++c) {
           const float4 f = ld_shared_f4(rbase + coff[c]);
@@ -362,7 +379,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // taps mode rewrites the stage in another layout: every converter has
       // read its row before any writes (the AND keeps an abort uniform)
-      if (!L::kSplit && taps) ok = named_bar_and(ok, 128, 2);
+      if (!L::kTmemA && taps) ok = named_bar_and(ok, 128, 2);
       if (!ok) break;
       if (kvalid < kBK) {
 #pragma unroll
@@ -373,6 +390,24 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < kBK / 4; ++c)
           st_shared_f4(rbase + swz128(row, c), v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+      }
+      if constexpr (L::kBf16) {
+        // bf16 pairs (lower k in the low half) into TMEM slot a, once the MMAs of
+        // the slot's previous use have completed (see the 3xTF32 case below)
+        if (item >= S2) {
+          const int prev = item - S2;
+          if (!mbar_wait(s1_empty(prev % S1), (prev / S1) & 1, abort_flag, p.status)) break;
+        }
+        uint32_t pk[kBK / 2];
+#pragma unroll
+        for (int e = 0; e < kBK / 2; ++e) {
+          const __nv_bfloat162 h2 = __floats2bfloat162_rn(v[2 * e], v[2 * e + 1]);
+          pk[e] = *reinterpret_cast<const uint32_t*>(&h2);
+        }
+        tc_fence_after();
+        tmem_st_32x32b_x16(tmem_base + lane_addr + L::kACol0 + a * L::kAStageCols, pk);
+        tmem_st_wait();
+        tc_fence_before();
       }
       if constexpr (L::kSplit) {
         // hi = trunc_tf32(v), lo = rna_tf32(v - hi) into TMEM slot a, once the
@@ -405,6 +440,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // indices: the MMA issue rate of this thread bounds the kernel.
     constexpr uint32_t idesc = make_idesc(2, kBM, BN);
     constexpr uint32_t idesc2 = make_idesc(2, kBM, 2 * BN);  // stacked B (BN = 64)
+    constexpr uint32_t idesc_bf = make_idesc(1, kBM, BN);    // bf16 x bf16
     if (lane == 0) {
       bool issued = false;
       uint32_t cc = 0;             // accumulation units started (chunks / tiles)
@@ -425,11 +461,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t ahi = tmem_base + L::kACol0 + a * L::kAStageCols;  // 3xTF32: A hi | lo
         const uint32_t alo = ahi + kBK;
         const uint64_t da = smem_desc_sw128(a_raw + s * L::kARaw);  // TF32: A as landed
-        const uint64_t dbh = smem_desc_sw128(b_hi + s * L::kBStride);
+        const uint64_t dbh = L::kBf16 ? smem_desc_sw64(b_hi + s * L::kBStride)
+                                       : smem_desc_sw128(b_hi + s * L::kBStride);
         uint64_t dbl = 0;
         if constexpr (L::kSplit) dbl = smem_desc_sw128(b_lo + s * L::kBStride);
+        if constexpr (L::kBf16) {
 #pragma unroll
-        for (int kk = 0; kk < kBK / 8; ++kk) {
+          for (int kk = 0; kk < kBK / 16; ++kk)  // K = 16 bf16 (32 bytes) per MMA
+            tc_mma_f16_ts(d_tmem, ahi + kk * 8, dbh + (uint64_t)(kk * 2), idesc_bf, (kin | kk) ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < (L::kBf16 ? 0 : kBK / 8); ++kk) {
           const uint32_t acc = (kin | kk) ? 1u : 0u;
           if constexpr (L::kStack) {
             // [hi.b_hi | hi.b_lo] over B hi and B lo rows, then lo.b_hi into the
@@ -753,6 +795,12 @@ int igemm3_launch(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap
     return short_k ? launch3_t<kPrecTF32, 128, 32, 4>(p, hi, lo, am, num_sms, st)
                    : launch3_t<kPrecTF32, 128, 32, 2>(p, hi, lo, am, num_sms, st);
   if (precision == kPrecTF32 && bn == 256) return launch3_t<kPrecTF32, 256, 32, 2>(p, hi, lo, am, num_sms, st);
+  if (precision == kPrecBF16 && bn == 64)
+    return short_k ? launch3_t<kPrecBF16, 64, 32, 4>(p, hi, lo, am, num_sms, st)
+                   : launch3_t<kPrecBF16, 64, 32, 2>(p, hi, lo, am, num_sms, st);
+  if (precision == kPrecBF16 && bn == 128)
+    return short_k ? launch3_t<kPrecBF16, 128, 32, 4>(p, hi, lo, am, num_sms, st)
+                   : launch3_t<kPrecBF16, 128, 32, 2>(p, hi, lo, am, num_sms, st);
   return (int)cudaErrorInvalidValue;
 }
 
