@@ -287,6 +287,15 @@ ONNXB200_API int onnxb200_graph_run(onnxb200_handle* h, onnxb200_graph* g,
 /* Same, from and to HOST buffers: copies in, runs, copies out, synchronizes. */
 ONNXB200_API int onnxb200_graph_run_host(onnxb200_handle* h, onnxb200_graph* g,
                                          const float* const* inputs, float* const* outputs);
+/* A sequence of n_batches host batches (inputs[b * n_inputs + i], outputs
+ * [b * n_outputs + i]; pinned host memory for the copies to overlap): batch b+1's
+ * host-to-device input copy runs on a copy stream as soon as batch b's graph has
+ * read its inputs, overlapping the rest of batch b.  Synchronizes at the end.
+ * The serving counterpart of calling ExecutionEngine::run once per batch
+ * (src/execution/engine.rs:166-231). */
+ONNXB200_API int onnxb200_graph_run_host_pipelined(onnxb200_handle* h, onnxb200_graph* g,
+                                                   int n_batches, const float* const* inputs,
+                                                   float* const* outputs);
 ONNXB200_API int onnxb200_graph_output_shape(const onnxb200_graph* g, int index, int64_t* shape,
                                              int* rank);
 

@@ -129,6 +129,7 @@ SIGNATURES = {
                                     ctypes.POINTER(_vp)]),
     "onnxb200_graph_run": (_int, [_vp, _vp, ctypes.POINTER(_vp), ctypes.POINTER(_vp)]),
     "onnxb200_graph_run_host": (_int, [_vp, _vp, ctypes.POINTER(_vp), ctypes.POINTER(_vp)]),
+    "onnxb200_graph_run_host_pipelined": (_int, [_vp, _vp, _int, ctypes.POINTER(_vp), ctypes.POINTER(_vp)]),
     "onnxb200_graph_output_shape": (_int, [_vp, _int, _i64p, ctypes.POINTER(_int)]),
     "onnxb200_graph_get_stats": (_int, [_vp, ctypes.POINTER(GraphStats)]),
     "onnxb200_graph_destroy": (_int, [_vp]),

@@ -10,7 +10,10 @@
 //           (first fit, largest first, over step lifetimes; the planner's
 //           optimize_memory_layout, src/memory/planner.rs:3554-3685).
 //   run:    the planned steps on the handle's stream; with use_cuda_graph the
-//           schedule is captured once into a CUDA graph and replayed.
+//           schedule after the input conversions is captured once into a CUDA
+//           graph and replayed (the conversions run eagerly, so new input
+//           pointers need no new capture, and a pipelined host run can start
+//           the next batch's input copy as soon as they are done).
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -141,12 +144,19 @@ struct onnxb200_graph {
   // CUDA graph state
   cudaGraph_t cg = nullptr;
   cudaGraphExec_t cge = nullptr;
-  std::vector<const void*> cap_in;
+  int64_t graph_kernels = 0;  // kernels inside the captured graph (all but the input conversions)
   std::vector<void*> cap_out;
   cudaStream_t cap_stream = nullptr;
   int runs = 0;
   // host-run staging
   std::vector<void*> dev_in, dev_out;
+  // Recorded in every run once the input-conversion steps (run eagerly, ahead
+  // of the captured graph) have read the user's input buffers: the pipelined
+  // host run copies the next batch into its staging buffers after this event.
+  cudaEvent_t ev_inputs_read = nullptr;
+  // pipelined host run: its own copy stream and events
+  cudaStream_t copy_stream = nullptr;
+  cudaEvent_t ev_copied = nullptr, ev_begin = nullptr, ev_copy_end = nullptr;
 };
 
 namespace {
@@ -179,6 +189,11 @@ void storage_view(const GTensor& t, std::vector<int64_t>& dims, std::vector<int6
 
 static void destroy_graph(onnxb200_graph* g) {
   if (!g) return;
+  if (g->ev_inputs_read) cudaEventDestroy(g->ev_inputs_read);
+  if (g->ev_copied) cudaEventDestroy(g->ev_copied);
+  if (g->ev_begin) cudaEventDestroy(g->ev_begin);
+  if (g->ev_copy_end) cudaEventDestroy(g->ev_copy_end);
+  if (g->copy_stream) cudaStreamDestroy(g->copy_stream);
   if (g->cge) cudaGraphExecDestroy(g->cge);
   if (g->cg) cudaGraphDestroy(g->cg);
   if (g->arena) cudaFree(g->arena);
@@ -211,6 +226,10 @@ extern "C" int onnxb200_graph_build(onnxb200_handle* h, const onnxb200_node* nod
   g->h = h;
   g->device = h->device;
   g->n_nodes_in = n_nodes;
+  if (cudaEventCreateWithFlags(&g->ev_inputs_read, cudaEventDisableTiming) != cudaSuccess) {
+    delete g;
+    return fail(h, ONNXB200_ERR_RESOURCE_EXHAUSTED, "graph event");
+  }
   std::map<std::string, int> by_name;
   auto tensor_id = [&](const std::string& name) -> int {
     auto it = by_name.find(name);
@@ -994,7 +1013,7 @@ extern "C" int onnxb200_graph_build(onnxb200_handle* h, const onnxb200_node* nod
 
 // ---------------------------------------------------------------------------------- run
 static int run_steps(onnxb200_graph* g, const float* const* uin, float* const* uout,
-                     std::vector<cudaEvent_t>* ev = nullptr) {
+                     std::vector<cudaEvent_t>* ev = nullptr, size_t first = 0, size_t last = SIZE_MAX) {
   onnxb200_handle* h = g->h;
   cudaStream_t st = h->stream;
   auto T = [&](int id) -> float* {
@@ -1003,7 +1022,8 @@ static int run_steps(onnxb200_graph* g, const float* const* uin, float* const* u
     return reinterpret_cast<float*>(g->arena + t.off);
   };
   int rc = 0;
-  for (size_t si = 0; si < g->steps.size(); ++si) {
+  last = std::min(last, g->steps.size());
+  for (size_t si = first; si < last; ++si) {
     const Step& s = g->steps[si];
     if (ev) cudaEventRecord((*ev)[2 * si], st);
     switch (s.type) {
@@ -1016,6 +1036,10 @@ static int run_steps(onnxb200_graph* g, const float* const* uin, float* const* u
         } else {
           rc = (int)cudaMemcpyAsync(T(s.out), uin[s.user_index], t.numel() * 4, cudaMemcpyDeviceToDevice, st);
         }
+        // the input conversions come first (and are never captured): after
+        // the last one the user's input buffers are free
+        if (!rc && (si + 1 == g->steps.size() || g->steps[si + 1].type != kInConvert))
+          rc = (int)cudaEventRecord(g->ev_inputs_read, st);
         break;
       }
       case kOutConvert: {
@@ -1207,7 +1231,6 @@ extern "C" int onnxb200_graph_run(onnxb200_handle* h, onnxb200_graph* g, const f
   if ((!inputs && !g->inputs.empty()) || (!outputs && !g->outputs.empty())) return ONNXB200_ERR_INVALID_ARGUMENT;
   cudaSetDevice(h->device);
   const bool use_graph = h->opts.use_cuda_graph != 0;
-  std::vector<const void*> vin(inputs, inputs + g->inputs.size());
   std::vector<void*> vout(outputs, outputs + g->outputs.size());
   if (!use_graph || g->runs == 0) {
     // eager run (the first one also counts the kernels of one run)
@@ -1218,13 +1241,21 @@ extern "C" int onnxb200_graph_run(onnxb200_handle* h, onnxb200_graph* g, const f
     g->runs++;
     return ONNXB200_OK;
   }
-  if (!g->cge || vin != g->cap_in || vout != g->cap_out || g->cap_stream != h->stream) {
+  // The input conversions run eagerly; the CUDA graph holds the remaining
+  // steps, so it depends on the output pointers only.
+  const size_t n_in = g->inputs.size();
+  {
+    int rc = run_steps(g, inputs, outputs, nullptr, 0, n_in);
+    if (rc) return rc;
+  }
+  if (!g->cge || vout != g->cap_out || g->cap_stream != h->stream) {
     if (g->cge) { cudaGraphExecDestroy(g->cge); g->cge = nullptr; }
     if (g->cg) { cudaGraphDestroy(g->cg); g->cg = nullptr; }
     cudaError_t e = cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal);
     if (e != cudaSuccess) return cuda_check(h, e, "graph capture begin");
     const int64_t l0 = h->launches;
-    int rc = run_steps(g, inputs, outputs);
+    int rc = run_steps(g, inputs, outputs, nullptr, n_in);
+    g->graph_kernels = h->launches - l0;
     h->launches = l0;  // counted when replayed
     cudaGraph_t cg = nullptr;
     e = cudaStreamEndCapture(h->stream, &cg);
@@ -1233,13 +1264,12 @@ extern "C" int onnxb200_graph_run(onnxb200_handle* h, onnxb200_graph* g, const f
     e = cudaGraphInstantiate(&g->cge, cg, 0);
     if (e != cudaSuccess) { cudaGraphDestroy(cg); return cuda_check(h, e, "graph instantiate"); }
     g->cg = cg;
-    g->cap_in = vin;
     g->cap_out = vout;
     g->cap_stream = h->stream;
   }
   cudaError_t e = cudaGraphLaunch(g->cge, h->stream);
   if (e != cudaSuccess) return cuda_check(h, e, "graph launch");
-  h->launches += g->kernels_per_run;
+  h->launches += g->graph_kernels;
   g->runs++;
   return ONNXB200_OK;
 }
@@ -1278,6 +1308,71 @@ extern "C" int onnxb200_graph_run_host(onnxb200_handle* h, onnxb200_graph* g, co
                                     cudaMemcpyDeviceToHost, h->stream);
     if (e != cudaSuccess) return cuda_check(h, e, "host run: output copy");
   }
+  return onnxb200_synchronize(h);
+}
+
+extern "C" int onnxb200_graph_run_host_pipelined(onnxb200_handle* h, onnxb200_graph* g, int n_batches,
+                                                 const float* const* inputs, float* const* outputs) {
+  if (!h || !g || g->h != h || n_batches < 0) return ONNXB200_ERR_INVALID_ARGUMENT;
+  if (n_batches == 0) return ONNXB200_OK;
+  if ((!inputs && !g->inputs.empty()) || (!outputs && !g->outputs.empty())) return ONNXB200_ERR_INVALID_ARGUMENT;
+  cudaSetDevice(h->device);
+  const size_t ni = g->inputs.size(), no = g->outputs.size();
+  if (g->dev_in.empty()) {  // the same staging buffers as onnxb200_graph_run_host
+    for (int id : g->inputs) {
+      void* p = nullptr;
+      if (cudaMalloc(&p, std::max<size_t>(g->tensors[id].numel() * 4, 4)) != cudaSuccess)
+        return fail(h, ONNXB200_ERR_RESOURCE_EXHAUSTED, "host run: input staging allocation");
+      g->dev_in.push_back(p);
+    }
+    for (int id : g->outputs) {
+      void* p = nullptr;
+      if (cudaMalloc(&p, std::max<size_t>(g->tensors[id].numel() * 4, 4)) != cudaSuccess)
+        return fail(h, ONNXB200_ERR_RESOURCE_EXHAUSTED, "host run: output staging allocation");
+      g->dev_out.push_back(p);
+    }
+  }
+  if (!g->copy_stream) {
+    if (cudaStreamCreateWithFlags(&g->copy_stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&g->ev_copied, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&g->ev_begin, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&g->ev_copy_end, cudaEventDisableTiming) != cudaSuccess)
+      return fail(h, ONNXB200_ERR_RESOURCE_EXHAUSTED, "pipelined host run: stream / events");
+  }
+  std::vector<const float*> din(ni);
+  std::vector<float*> dout(no);
+  for (size_t i = 0; i < ni; ++i) din[i] = static_cast<const float*>(g->dev_in[i]);
+  for (size_t i = 0; i < no; ++i) dout[i] = static_cast<float*>(g->dev_out[i]);
+  cudaStream_t cs = g->copy_stream;
+  // everything already queued on the handle's stream comes first
+  cudaError_t e = cudaEventRecord(g->ev_begin, h->stream);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, g->ev_begin, 0);
+  if (e != cudaSuccess) return cuda_check(h, e, "pipelined host run: ordering");
+  for (int b = 0; b < n_batches; ++b) {
+    // batch b's input: into the staging buffers once the previous batch's
+    // graph has read them (its input-conversion steps), overlapping the rest
+    // of that graph
+    if (b > 0) e = cudaStreamWaitEvent(cs, g->ev_inputs_read, 0);
+    for (size_t i = 0; i < ni && e == cudaSuccess; ++i)
+      e = cudaMemcpyAsync(g->dev_in[i], inputs[b * ni + i], g->tensors[g->inputs[i]].numel() * 4,
+                          cudaMemcpyHostToDevice, cs);
+    if (e == cudaSuccess) e = cudaEventRecord(g->ev_copied, cs);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(h->stream, g->ev_copied, 0);
+    if (e != cudaSuccess) return cuda_check(h, e, "pipelined host run: input copy");
+    int rc = onnxb200_graph_run(h, g, din.data(), dout.data());
+    if (rc) return rc;
+    // the (small) outputs on the handle's stream, before the next batch's
+    // graph rewrites the output staging buffers
+    for (size_t i = 0; i < no; ++i) {
+      e = cudaMemcpyAsync(outputs[b * no + i], g->dev_out[i], g->tensors[g->outputs[i]].numel() * 4,
+                          cudaMemcpyDeviceToHost, h->stream);
+      if (e != cudaSuccess) return cuda_check(h, e, "pipelined host run: output copy");
+    }
+  }
+  // the handle's stream ends after the copy stream's last work
+  e = cudaEventRecord(g->ev_copy_end, cs);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(h->stream, g->ev_copy_end, 0);
+  if (e != cudaSuccess) return cuda_check(h, e, "pipelined host run: ordering");
   return onnxb200_synchronize(h);
 }
 

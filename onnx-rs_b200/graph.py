@@ -139,6 +139,26 @@ class Graph:
         self.handle.check(C.lib().onnxb200_graph_run_host(self.handle.ptr, self.ptr, iarr, oarr), "graph run_host")
         return list(outputs)
 
+    def run_host_pipelined(self, batches: Sequence[Sequence[np.ndarray | torch.Tensor]],
+                           outputs: Sequence[Sequence[np.ndarray | torch.Tensor]] | None = None):
+        """Several host batches in a row (onnxb200_graph_run_host_pipelined): each
+        batch's input copy overlaps the previous batch's compute.  Host buffers
+        should be pinned (torch ``pin_memory()``) for the copies to overlap."""
+        def addr(t):
+            return t.ctypes.data if isinstance(t, np.ndarray) else t.data_ptr()
+
+        ins = [[np.ascontiguousarray(x, dtype=np.float32) if isinstance(x, np.ndarray) else x for x in b]
+               for b in batches]
+        if outputs is None:
+            outputs = [[np.empty(s, np.float32) for s in self.output_shapes] for _ in ins]
+        flat_in = [addr(t) for b in ins for t in b]
+        flat_out = [addr(t) for b in outputs for t in b]
+        iarr = (ctypes.c_void_p * max(1, len(flat_in)))(*flat_in)
+        oarr = (ctypes.c_void_p * max(1, len(flat_out)))(*flat_out)
+        self.handle.check(C.lib().onnxb200_graph_run_host_pipelined(self.handle.ptr, self.ptr, len(ins), iarr, oarr),
+                          "graph run_host_pipelined")
+        return [list(o) for o in outputs]
+
     def profile(self, inputs: Sequence[torch.Tensor], outputs: Sequence[torch.Tensor] | None = None) -> List[dict]:
         """One eager run with CUDA events around every step; returns per-step
         {kind, ms, flops, bytes} (algorithmic work)."""

@@ -52,6 +52,16 @@ def test_resnet18_graph(ob, r18_ref, precision, tol):
     # host buffers in / out
     yh = g.run_host([x])[0]
     np.testing.assert_array_equal(yh, y_replay.cpu().numpy())
+    # a pipelined sequence of host batches (each input copy overlaps the
+    # previous batch's compute): every batch as if run alone
+    xs = [x, (x * 0.5).astype(np.float32), x[::-1].copy()]
+    pinned = [torch.from_numpy(v).pin_memory() for v in xs]
+    outs = [[torch.empty(list(y_replay.shape), dtype=torch.float32).pin_memory()] for _ in xs]
+    g.run_host_pipelined([[t] for t in pinned], outs)
+    for v, o in zip(xs, outs):
+        single = g.run([torch.from_numpy(v).cuda()])[0]
+        h.synchronize()
+        np.testing.assert_array_equal(o[0].numpy(), single.cpu().numpy())
     assert g.stats()["captured"] == 1
     g.close()
     h.close()
