@@ -107,28 +107,33 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(rows)}
 
 
-def cpu_baseline(steps=1, images=None):
-    """Oracle ResNet-50 (3xTF32 path's reference semantics, fp32) on host cores."""
-    import numpy as np
+def cpu_baseline(steps=1, images=None, min_seconds=0.0, max_steps=8):
+    """Oracle ResNet-50 (3xTF32 path's reference semantics, fp32) on host cores:
+    every host thread this process may use (at most 64, so that the sample's
+    activations stay a few GB), one image per thread; at least `steps` runs and
+    more (up to `max_steps`) until `min_seconds` of work have been timed."""
     import importlib
     from oracle import oracle as orc
     ob = importlib.import_module("onnx-rs_b200")
     orc.build()
-    cores = os.cpu_count() or 1
-    threads = max(1, min(cores, 8))
+    try:
+        avail = len(os.sched_getaffinity(0))
+    except AttributeError:
+        avail = os.cpu_count() or 1
+    threads = max(1, min(avail, 64))
     n = images or threads
     nodes, inits, ins, outs = ob.workloads.resnet50(batch=n, seed=SEED)
     x = ob.workloads.resnet_input(SEED, n)
     times = []
-    for _ in range(steps):
+    while len(times) < steps or (sum(times) < min_seconds and len(times) < max_steps):
         t0 = time.perf_counter()
         orc.run_graph(nodes, inits, {"X": x}, outs, nthreads=threads)
         times.append(time.perf_counter() - t0)
     t = statistics.median(times)
     return {"value": n / t, "unit": "images/s", "cores": threads, "kind": "port",
             "sample": f"ResNet-50 v1.5 batch {n} (of 256), seed {SEED}, oracle C restatement of the reference's "
-                      f"CPU operators (im2col+GEMM / direct conv, batch split over {threads} threads), "
-                      f"median of {steps} run(s), {t:.2f} s each"}
+                      f"CPU operators (im2col+GEMM / direct conv, batch split over {threads} of {avail} "
+                      f"available host threads), median of {len(times)} run(s), {t:.2f} s each"}
 
 
 def run_reference(args):
@@ -434,7 +439,7 @@ def main():
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
-            cpu = cpu_baseline(steps=1)
+            cpu = cpu_baseline(steps=1, min_seconds=10.0)
         line = {
             "metric": METRIC if args.precision == "3xtf32" else METRIC_FAST[args.precision],
             "value": value, "unit": "images/s", "n_gpus": world, "steps": args.steps,
