@@ -48,6 +48,9 @@ extern "C" {
 #define ONNXB200_ERR_INVALID_OPERATOR 7   /* Error::InvalidOperator */
 #define ONNXB200_ERR_CANCELLED 8          /* Error::ExecutionCancelled */
 #define ONNXB200_ERR_INVALID_ARGUMENT 9   /* null handle / pointer */
+#define ONNXB200_ERR_IO 10                /* Error::IoError / Error::ModelLoadError */
+#define ONNXB200_ERR_PROTOBUF 11          /* Error::ProtobufError (malformed model bytes) */
+#define ONNXB200_ERR_INVALID_MODEL 12     /* Error::InvalidModel / Error::MissingField */
 #endif
 
 /* ---------------------------------------------------------------- enums */
@@ -322,6 +325,52 @@ ONNXB200_API int onnxb200_graph_profile(onnxb200_handle* h, onnxb200_graph* g,
                                         onnxb200_step_profile* steps, int max_steps, int* n_steps);
 ONNXB200_API int onnxb200_graph_get_stats(const onnxb200_graph* g, onnxb200_graph_stats* st);
 ONNXB200_API int onnxb200_graph_destroy(onnxb200_graph* g);
+
+/* ---------------------------------------------------------------- ONNX models */
+/* A parsed .onnx ModelProto, host memory only (no handle, no GPU needed):
+ * OnnxModelLoader (src/parser/model_loader.rs:27-454) restricted to the main
+ * graph -- nodes with INT / FLOAT / STRING / INTS attributes (others are counted
+ * and skipped), fp32 initializers (inline raw_data / float_data, or external
+ * data next to the model file; other element types are counted and skipped),
+ * graph inputs that are not initializers (symbolic dimensions read as -1) and
+ * graph outputs.  Errors: ONNXB200_ERR_PROTOBUF (malformed bytes),
+ * ONNXB200_ERR_INVALID_MODEL (no graph, undefined attribute type, a value
+ * without a type, data that does not match its shape), ONNXB200_ERR_IO,
+ * ONNXB200_ERR_UNSUPPORTED (segmented tensors; external data when parsing
+ * from memory without base_dir); the message goes to err (may be NULL). */
+typedef struct onnxb200_model onnxb200_model;
+typedef struct onnxb200_model_info {
+  int64_t ir_version;
+  int64_t opset;                  /* version imported for the default domain (1 if none) */
+  int n_nodes;
+  int n_initializers;             /* fp32 initializers */
+  int n_skipped_initializers;     /* initializers of other element types */
+  int n_skipped_attributes;       /* attributes with no onnxb200_attr form */
+  int n_inputs;                   /* graph inputs that are not initializers */
+  int n_outputs;
+  const char* producer_name;
+  const char* graph_name;
+} onnxb200_model_info;
+/* OnnxModelLoader::load_model_from_bytes (model_loader.rs:40-43); base_dir
+ * (may be NULL) is where external data files are looked up. */
+ONNXB200_API int onnxb200_model_parse(const void* data, size_t len, const char* base_dir,
+                                      onnxb200_model** out, char* err, size_t err_len);
+/* OnnxModelLoader::load_model (model_loader.rs:27-37). */
+ONNXB200_API int onnxb200_model_load(const char* path, onnxb200_model** out, char* err, size_t err_len);
+ONNXB200_API int onnxb200_model_get_info(const onnxb200_model* m, onnxb200_model_info* info);
+/* Views into the model (valid until onnxb200_model_destroy), in the forms
+ * onnxb200_graph_build takes. */
+ONNXB200_API int onnxb200_model_get_nodes(const onnxb200_model* m, const onnxb200_node** nodes, int* n);
+ONNXB200_API int onnxb200_model_get_initializers(const onnxb200_model* m, const onnxb200_tensor_info** t,
+                                                 int* n);
+ONNXB200_API int onnxb200_model_get_inputs(const onnxb200_model* m, const onnxb200_tensor_info** t, int* n);
+ONNXB200_API int onnxb200_model_get_outputs(const onnxb200_model* m, const char* const** names, int* n);
+ONNXB200_API int onnxb200_model_destroy(onnxb200_model* m);
+/* onnxb200_graph_build over a parsed model; input_shapes (matched by name)
+ * replace the model's input shapes, which must then all be concrete. */
+ONNXB200_API int onnxb200_graph_build_from_model(onnxb200_handle* h, const onnxb200_model* m,
+                                                 const onnxb200_tensor_info* input_shapes,
+                                                 int n_input_shapes, onnxb200_graph** out);
 
 #ifdef __cplusplus
 }

@@ -8,15 +8,17 @@ reference's operator interface over that ABI.  Import it with
 """
 from . import _capi
 from .runtime import (Handle, OnnxB200Error, ValidationError, ExecutionError, UnsupportedFeature,
-                      OperationTimeout, ResourceExhausted, InvalidGraph, InvalidOperator)
+                      OperationTimeout, ResourceExhausted, InvalidGraph, InvalidOperator, IoError, ProtobufError,
+                      InvalidModel)
 from .ops import (ExecutionContext, Operator, OperatorRegistry, Conv, ConvPlan, MatMul, Gemm, MaxPool,
                   GlobalAveragePool, Relu, Add, BatchNormalization, Flatten)
 from .graph import Graph
-from . import sharding, synth, workloads
+from . import onnx_io, sharding, synth, workloads
 
 LIB_PATH = _capi.LIB_PATH
 
 __all__ = ["Handle", "OnnxB200Error", "ValidationError", "ExecutionError", "UnsupportedFeature",
            "OperationTimeout", "ResourceExhausted", "InvalidGraph", "InvalidOperator", "ExecutionContext",
            "Operator", "OperatorRegistry", "Conv", "ConvPlan", "MatMul", "Gemm", "MaxPool", "GlobalAveragePool", "Relu",
-           "Add", "BatchNormalization", "Flatten", "Graph", "synth", "workloads", "LIB_PATH"]
+           "Add", "BatchNormalization", "Flatten", "Graph", "onnx_io", "synth", "workloads", "LIB_PATH",
+           "IoError", "ProtobufError", "InvalidModel"]

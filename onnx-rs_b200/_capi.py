@@ -22,6 +22,9 @@ ERR_INVALID_GRAPH = 6
 ERR_INVALID_OPERATOR = 7
 ERR_CANCELLED = 8
 ERR_INVALID_ARGUMENT = 9
+ERR_IO = 10
+ERR_PROTOBUF = 11
+ERR_INVALID_MODEL = 12
 
 PREC_DEFAULT = -1
 PREC_3XTF32 = 0
@@ -88,6 +91,13 @@ class GraphStats(ctypes.Structure):
                 ("weight_bytes", ctypes.c_int64), ("captured", ctypes.c_int)]
 
 
+class ModelInfo(ctypes.Structure):
+    _fields_ = [("ir_version", ctypes.c_int64), ("opset", ctypes.c_int64), ("n_nodes", ctypes.c_int),
+                ("n_initializers", ctypes.c_int), ("n_skipped_initializers", ctypes.c_int),
+                ("n_skipped_attributes", ctypes.c_int), ("n_inputs", ctypes.c_int), ("n_outputs", ctypes.c_int),
+                ("producer_name", ctypes.c_char_p), ("graph_name", ctypes.c_char_p)]
+
+
 _vp = ctypes.c_void_p
 _i64 = ctypes.c_int64
 _i64p = ctypes.POINTER(ctypes.c_int64)
@@ -135,6 +145,18 @@ SIGNATURES = {
     "onnxb200_graph_destroy": (_int, [_vp]),
     "onnxb200_graph_profile": (_int, [_vp, _vp, ctypes.POINTER(_vp), ctypes.POINTER(_vp),
                                       ctypes.POINTER(StepProfile), _int, ctypes.POINTER(_int)]),
+    "onnxb200_model_parse": (_int, [_vp, ctypes.c_size_t, ctypes.c_char_p, ctypes.POINTER(_vp), ctypes.c_char_p,
+                                    ctypes.c_size_t]),
+    "onnxb200_model_load": (_int, [ctypes.c_char_p, ctypes.POINTER(_vp), ctypes.c_char_p, ctypes.c_size_t]),
+    "onnxb200_model_get_info": (_int, [_vp, ctypes.POINTER(ModelInfo)]),
+    "onnxb200_model_get_nodes": (_int, [_vp, ctypes.POINTER(ctypes.POINTER(Node)), ctypes.POINTER(_int)]),
+    "onnxb200_model_get_initializers": (_int, [_vp, ctypes.POINTER(ctypes.POINTER(TensorInfo)),
+                                               ctypes.POINTER(_int)]),
+    "onnxb200_model_get_inputs": (_int, [_vp, ctypes.POINTER(ctypes.POINTER(TensorInfo)), ctypes.POINTER(_int)]),
+    "onnxb200_model_get_outputs": (_int, [_vp, ctypes.POINTER(ctypes.POINTER(ctypes.c_char_p)),
+                                          ctypes.POINTER(_int)]),
+    "onnxb200_model_destroy": (_int, [_vp]),
+    "onnxb200_graph_build_from_model": (_int, [_vp, _vp, ctypes.POINTER(TensorInfo), _int, ctypes.POINTER(_vp)]),
 }
 
 _lib = None

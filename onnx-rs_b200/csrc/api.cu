@@ -419,6 +419,9 @@ const char* onnxb200_status_string(int s) {
     case ONNXB200_ERR_INVALID_OPERATOR: return "invalid operator";
     case ONNXB200_ERR_CANCELLED: return "execution cancelled";
     case ONNXB200_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case ONNXB200_ERR_IO: return "I/O error";
+    case ONNXB200_ERR_PROTOBUF: return "protobuf parsing error";
+    case ONNXB200_ERR_INVALID_MODEL: return "invalid ONNX model";
     default: return "unknown status";
   }
 }

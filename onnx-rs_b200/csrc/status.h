@@ -13,3 +13,6 @@
 #define ONNXB200_ERR_INVALID_OPERATOR 7   /* Error::InvalidOperator (op not in registry) */
 #define ONNXB200_ERR_CANCELLED 8          /* Error::ExecutionCancelled */
 #define ONNXB200_ERR_INVALID_ARGUMENT 9   /* null handle / pointer (no reference variant) */
+#define ONNXB200_ERR_IO 10                /* Error::IoError / Error::ModelLoadError */
+#define ONNXB200_ERR_PROTOBUF 11          /* Error::ProtobufError (malformed model bytes) */
+#define ONNXB200_ERR_INVALID_MODEL 12     /* Error::InvalidModel / Error::MissingField */

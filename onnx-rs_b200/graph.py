@@ -97,12 +97,42 @@ class Graph:
         handle.check(C.lib().onnxb200_graph_build(handle.ptr, cnodes, len(nodes), init_arr, len(inits), in_arr,
                                                   len(ins), out_arr, len(onames), ctypes.byref(ptr)), "graph build")
         self.ptr = ptr
+        self._read_output_shapes()
+
+    def _read_output_shapes(self):
         self.output_shapes = []
-        for i in range(len(outputs)):
+        for i in range(len(self.output_names)):
             shp = C.i64_array([0] * 8)
             r = ctypes.c_int()
-            handle.check(C.lib().onnxb200_graph_output_shape(self.ptr, i, shp, ctypes.byref(r)))
+            self.handle.check(C.lib().onnxb200_graph_output_shape(self.ptr, i, shp, ctypes.byref(r)))
             self.output_shapes.append([int(v) for v in shp[:r.value]])
+
+    @classmethod
+    def from_model(cls, handle: Handle, model, input_shapes: Dict[str, Sequence[int]] | None = None) -> "Graph":
+        """onnxb200_graph_build_from_model: the graph of a parsed .onnx model
+        (``onnx_io.load``); ``input_shapes`` fixes symbolic input dimensions."""
+        input_shapes = dict(input_shapes or {})
+        keep: list = []
+        over = []
+        for name, shape in input_shapes.items():
+            t = C.TensorInfo()
+            t.name = name.encode()
+            shp = C.i64_array(shape)
+            keep += [t.name, shp]
+            t.shape = ctypes.cast(shp, ctypes.POINTER(ctypes.c_int64))
+            t.rank = len(shape)
+            over.append(t)
+        arr = (C.TensorInfo * max(1, len(over)))(*over)
+        ptr = ctypes.c_void_p()
+        handle.check(C.lib().onnxb200_graph_build_from_model(handle.ptr, model.ptr, arr, len(over), ctypes.byref(ptr)),
+                     "graph build from model")
+        g = cls.__new__(cls)
+        g.handle = handle
+        g.input_specs = [(n, list(input_shapes.get(n, s))) for n, s in model.inputs]
+        g.output_names = model.outputs
+        g.ptr = ptr
+        g._read_output_shapes()
+        return g
 
     def stats(self) -> dict:
         s = C.GraphStats()

@@ -49,10 +49,23 @@ class InvalidOperator(OnnxB200Error):
     pass
 
 
+class IoError(OnnxB200Error):
+    pass
+
+
+class ProtobufError(OnnxB200Error):
+    pass
+
+
+class InvalidModel(OnnxB200Error):
+    pass
+
+
 _ERRORS = {
     C.ERR_VALIDATION: ValidationError, C.ERR_EXECUTION: ExecutionError, C.ERR_UNSUPPORTED: UnsupportedFeature,
     C.ERR_TIMEOUT: OperationTimeout, C.ERR_RESOURCE_EXHAUSTED: ResourceExhausted,
     C.ERR_INVALID_GRAPH: InvalidGraph, C.ERR_INVALID_OPERATOR: InvalidOperator,
+    C.ERR_IO: IoError, C.ERR_PROTOBUF: ProtobufError, C.ERR_INVALID_MODEL: InvalidModel,
 }
 
 

@@ -67,6 +67,32 @@ def test_resnet18_graph(ob, r18_ref, precision, tol):
     h.close()
 
 
+def test_graph_from_onnx_model(ob, r18_ref, tmp_path):
+    """A .onnx file (weights in an external data file, symbolic batch
+    dimension) read by onnxb200_model_load and built by
+    onnxb200_graph_build_from_model runs exactly like the node-list graph."""
+    nodes, inits, ins, outs, x, ref = r18_ref
+    h = ob.Handle(0, precision="3xtf32")
+    g_nodes = ob.Graph(h, nodes, inits, ins, outs)
+    xin = torch.from_numpy(x).cuda()
+    y_nodes = g_nodes.run([xin])[0].cpu().numpy()
+    path = str(tmp_path / "resnet18.onnx")
+    ob.onnx_io.save(path, nodes, inits, [("X", ["batch", 3, 224, 224])], outs, external_data=True)
+    m = ob.onnx_io.load(path)
+    assert m.inputs == [("X", [-1, 3, 224, 224])]
+    with pytest.raises(ob.ValidationError):
+        ob.Graph.from_model(h, m)  # symbolic batch and no shape given
+    g = ob.Graph.from_model(h, m, {"X": list(x.shape)})
+    assert g.output_shapes == g_nodes.output_shapes
+    assert g.stats()["n_fused"] == g_nodes.stats()["n_fused"]
+    y = g.run([xin])[0].cpu().numpy()
+    np.testing.assert_array_equal(y, y_nodes)
+    check_logits(y, ref, 1e-3, "resnet18 from .onnx")
+    g.close()
+    g_nodes.close()
+    h.close()
+
+
 def test_resnet18_full_batch_config(ob, oracle, r18_ref):
     """ResNet-18 at batch 32 (seed 2): images 0 and 31 against the oracle."""
     nodes, inits, ins, outs = ob.workloads.resnet18(batch=32, seed=2)
