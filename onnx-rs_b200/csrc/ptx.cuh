@@ -365,12 +365,18 @@ __host__ __device__ constexpr uint32_t make_idesc(int ab_format, int m, int n) {
 }
 
 // ---------------------------------------------------------------- rounding
-// fp32 -> tf32, round to nearest (ties away), result kept in a 32-bit container
-// with the 13 low mantissa bits zero.
+// fp32 -> tf32, round to nearest with ties away from zero, result kept in a
+// 32-bit container with the 13 low mantissa bits zero.  Done on the integer
+// pipes: adding half a tf32 unit in the last place (bit 12) to the sign-magnitude
+// bit pattern rounds the magnitude half away from zero, carrying into the
+// exponent when the mantissa overflows (up to infinity past the largest
+// finite tf32), and the mask drops the 13 low bits.  For every finite input
+// this is the ties-away rounding of the IEEE-754 format; NaN stays NaN when a
+// payload bit above bit 12 is set, as for every NaN an fp32 operation returns.
+// (The conversion instruction for this rounding issues on the narrow
+// transcendental pipe, which bounded the 3xTF32 converter warps.)
 __device__ __forceinline__ float to_tf32(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return __uint_as_float(r);
+  return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
 }
 
 // fp32 -> tf32 by truncation (the 13 low mantissa bits cleared): the value a
