@@ -128,6 +128,27 @@ typedef struct onnxb200_conv_desc {
 /* Conv::output_shapes (src/ops/nn/conv.rs:205-323): out[4] = N, C_out, OH, OW. */
 ONNXB200_API int onnxb200_conv2d_output_shape(const onnxb200_conv_desc* d, int64_t out[4]);
 
+/* 1-D, 2-D and 3-D Conv (compute_conv, src/ops/nn/conv.rs:534-606; spatial
+ * dims of 1-D in[0] = L, of 2-D in = {H, W}, of 3-D in = {D, H, W}, likewise the
+ * other arrays).  x / y are NCL, NCHW or NCDHW; w is [c_out][c/group][k...];
+ * bias [c_out] or NULL; relu != 0 fuses Relu.  1-D runs as a 2-D convolution of
+ * height 1 on the tensor-core path (the handle's precision); 3-D runs on CUDA
+ * cores in fp32 (compute_conv3d_direct_impl, conv.rs:938-1038). */
+typedef struct onnxb200_conv_nd_desc {
+  int spatial;                 /* 1, 2 or 3 */
+  int64_t n, c, c_out, group;  /* group 0 = 1 */
+  int64_t in[3], kernel[3];
+  int64_t stride[3];           /* 0 = 1 */
+  int64_t pad_begin[3], pad_end[3];
+  int64_t dilation[3];         /* 0 = 1 */
+  int auto_pad;                /* ONNXB200_AUTOPAD_* */
+  int relu;
+} onnxb200_conv_nd_desc;
+/* Conv::output_shapes (conv.rs:205-323) for 1 to 3 spatial dims: out[0..rank). */
+ONNXB200_API int onnxb200_conv_nd_output_shape(const onnxb200_conv_nd_desc* d, int64_t out[5], int* rank);
+ONNXB200_API int onnxb200_conv_nd(onnxb200_handle* h, const onnxb200_conv_nd_desc* d, const float* x,
+                                  const float* w, const float* bias, float* y);
+
 /* Conv::compute (src/ops/nn/conv.rs:156-203 -> compute_conv :534-606) with the
  * optional fused epilogue.  w is OIHW; bias [c_out] if EPI_BIAS; bn_* [c_out]
  * (ONNX scale, B, mean, var) if EPI_BN; residual shaped like y if EPI_RESIDUAL.

@@ -59,6 +59,13 @@ class ConvDesc(ctypes.Structure):
         ("precision", ctypes.c_int), ("bn_epsilon", ctypes.c_float)]
 
 
+class ConvNdDesc(ctypes.Structure):
+    _fields_ = [("spatial", ctypes.c_int), ("n", ctypes.c_int64), ("c", ctypes.c_int64),
+                ("c_out", ctypes.c_int64), ("group", ctypes.c_int64)] + [
+        (f, ctypes.c_int64 * 3) for f in ("in_", "kernel", "stride", "pad_begin", "pad_end", "dilation")] + [
+        ("auto_pad", ctypes.c_int), ("relu", ctypes.c_int)]
+
+
 class Attr(ctypes.Structure):
     _fields_ = [("name", ctypes.c_char_p), ("type", ctypes.c_int), ("i", ctypes.c_int64),
                 ("f", ctypes.c_float), ("ints", ctypes.POINTER(ctypes.c_int64)), ("n_ints", ctypes.c_int),
@@ -122,6 +129,8 @@ SIGNATURES = {
     "onnxb200_conv_plan_create": (_int, [_vp, ctypes.POINTER(ConvDesc)] + [_vp] * 6 + [ctypes.POINTER(_vp)]),
     "onnxb200_conv_plan_run": (_int, [_vp, _vp, _vp, _vp, _vp]),
     "onnxb200_conv_plan_destroy": (_int, [_vp]),
+    "onnxb200_conv_nd_output_shape": (_int, [ctypes.POINTER(ConvNdDesc), _i64p, ctypes.POINTER(_int)]),
+    "onnxb200_conv_nd": (_int, [_vp, ctypes.POINTER(ConvNdDesc), _vp, _vp, _vp, _vp]),
     "onnxb200_conv2d_nhwc_noalloc": (_int, [_vp, ctypes.POINTER(ConvDesc)] + [_vp] * 9),
     "onnxb200_matmul_output_shape": (_int, [_i64p, _int, _i64p, _int, _i64p, ctypes.POINTER(_int)]),
     "onnxb200_matmul": (_int, [_vp, _vp, _i64p, _int, _vp, _i64p, _int, _vp, _int, _int, _vp]),

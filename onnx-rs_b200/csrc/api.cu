@@ -614,6 +614,148 @@ int onnxb200_conv_plan_run(onnxb200_handle* h, const onnxb200_conv_plan* p, cons
   return conv_run_layout(h, p, x, residual, y, 0);
 }
 
+// ---------------------------------------------------------------- 1-D / 2-D / 3-D
+namespace {
+// Resolved geometry of an N-d convolution (spatial dims padded to 3 with ones
+// in front: 1-D is [1, 1, L], 2-D is [1, H, W]).
+struct ConvNd {
+  int sp;
+  int64_t n, c, co, g;
+  int64_t in[3], k[3], s[3], pb[3], pe[3], dl[3], out[3];
+};
+
+int resolve_conv_nd(onnxb200_handle* h, const onnxb200_conv_nd_desc* d, ConvNd* r) {
+  if (!d) return set_error(h, ONNXB200_ERR_INVALID_ARGUMENT, "null conv descriptor");
+  // compute_conv (src/ops/nn/conv.rs:546-565): rank 3 to 5 (1 to 3 spatial dims)
+  if (d->spatial < 1 || d->spatial > 3)
+    return set_error(h, ONNXB200_ERR_VALIDATION, "Conv supports only 1D, 2D, and 3D convolutions");
+  r->sp = d->spatial;
+  r->n = d->n;
+  r->c = d->c;
+  r->co = d->c_out;
+  r->g = d->group > 0 ? d->group : 1;
+  if (r->n < 0 || r->c <= 0 || r->co <= 0) return set_error(h, ONNXB200_ERR_VALIDATION, "Conv: non-positive dimension");
+  if (r->c % r->g != 0 || r->co % r->g != 0)
+    return set_error(h, ONNXB200_ERR_VALIDATION, "Input and output channels must be divisible by groups");
+  const int off = 3 - r->sp;
+  for (int i = 0; i < 3; ++i) {
+    const int j = i - off;  // index into the descriptor's arrays
+    const bool used = j >= 0;
+    r->in[i] = used ? d->in[j] : 1;
+    r->k[i] = used ? d->kernel[j] : 1;
+    r->s[i] = used && d->stride[j] > 0 ? d->stride[j] : 1;
+    r->dl[i] = used && d->dilation[j] > 0 ? d->dilation[j] : 1;
+    r->pb[i] = used ? d->pad_begin[j] : 0;
+    r->pe[i] = used ? d->pad_end[j] : 0;
+    if (r->in[i] <= 0 || r->k[i] <= 0) return set_error(h, ONNXB200_ERR_VALIDATION, "Conv: non-positive dimension");
+    if (used && (d->auto_pad == ONNXB200_AUTOPAD_SAME_UPPER || d->auto_pad == ONNXB200_AUTOPAD_SAME_LOWER)) {
+      // calculate_same_padding (src/ops/nn/conv.rs:426-458)
+      const int64_t dk = (r->k[i] - 1) * r->dl[i] + 1;
+      const int64_t o = (r->in[i] + r->s[i] - 1) / r->s[i];
+      const int64_t need = (o - 1) * r->s[i] + dk - r->in[i];
+      const int64_t half = need > 0 ? need / 2 : 0, rest = need > 0 ? need - half : 0;
+      r->pb[i] = d->auto_pad == ONNXB200_AUTOPAD_SAME_UPPER ? half : rest;
+      r->pe[i] = d->auto_pad == ONNXB200_AUTOPAD_SAME_UPPER ? rest : half;
+    } else if (d->auto_pad == ONNXB200_AUTOPAD_VALID) {
+      r->pb[i] = r->pe[i] = 0;
+    } else if (d->auto_pad != ONNXB200_AUTOPAD_NOTSET && d->auto_pad != ONNXB200_AUTOPAD_SAME_UPPER &&
+               d->auto_pad != ONNXB200_AUTOPAD_SAME_LOWER) {
+      return set_error(h, ONNXB200_ERR_VALIDATION, "Conv: unknown auto_pad");
+    }
+    if (r->pb[i] < 0 || r->pe[i] < 0) return set_error(h, ONNXB200_ERR_VALIDATION, "Conv: negative padding");
+    r->out[i] = conv_out_dim(r->in[i], r->k[i], r->s[i], r->pb[i], r->pe[i], r->dl[i]);
+    if (r->out[i] <= 0) return set_error(h, ONNXB200_ERR_VALIDATION, "Conv: kernel larger than padded input");
+  }
+  int64_t in_el = r->n * r->c, out_el = r->n * r->co;
+  for (int i = 0; i < 3; ++i) {
+    in_el *= r->in[i];
+    out_el *= r->out[i];
+  }
+  if (in_el > (int64_t)INT32_MAX * 4 || out_el > (int64_t)INT32_MAX * 4 ||
+      r->co * (r->c / r->g) * r->k[0] * r->k[1] * r->k[2] > (int64_t)INT32_MAX)
+    return set_error(h, ONNXB200_ERR_UNSUPPORTED, "Conv: tensor too large");
+  return ONNXB200_OK;
+}
+}  // namespace
+
+int onnxb200_conv_nd_output_shape(const onnxb200_conv_nd_desc* d, int64_t out[5], int* rank) {
+  if (!d || !out || !rank) return ONNXB200_ERR_INVALID_ARGUMENT;
+  onnxb200_handle tmp;
+  ConvNd r;
+  int rc = resolve_conv_nd(&tmp, d, &r);
+  if (rc) return rc;
+  *rank = r.sp + 2;
+  out[0] = r.n;
+  out[1] = r.co;
+  for (int i = 0; i < r.sp; ++i) out[2 + i] = r.out[3 - r.sp + i];
+  return ONNXB200_OK;
+}
+
+int onnxb200_conv_nd(onnxb200_handle* h, const onnxb200_conv_nd_desc* d, const float* x, const float* w,
+                     const float* bias, float* y) {
+  if (!h || !d) return set_error(h, ONNXB200_ERR_INVALID_ARGUMENT, "Conv: null argument");
+  cudaSetDevice(h->device);
+  ConvNd r;
+  int rc = resolve_conv_nd(h, d, &r);
+  if (rc) return rc;
+  if (r.n == 0) return ONNXB200_OK;
+  if (!x || !w || !y) return set_error(h, ONNXB200_ERR_INVALID_ARGUMENT, "Conv: null argument");
+  if (r.sp <= 2) {
+    // 1-D (NCL) is the 2-D convolution of an [N, C, 1, L] tensor with [CO, C/g, 1, k]
+    // filters: the same memory, run on the tensor-core path
+    onnxb200_conv_desc c{};
+    c.n = r.n;
+    c.c = r.c;
+    c.h = r.in[1];
+    c.w = r.in[2];
+    c.c_out = r.co;
+    c.kh = r.k[1];
+    c.kw = r.k[2];
+    c.stride_h = r.s[1];
+    c.stride_w = r.s[2];
+    c.pad_top = r.pb[1];
+    c.pad_left = r.pb[2];
+    c.pad_bottom = r.pe[1];
+    c.pad_right = r.pe[2];
+    c.dil_h = r.dl[1];
+    c.dil_w = r.dl[2];
+    c.group = r.g;
+    c.auto_pad = ONNXB200_AUTOPAD_NOTSET;
+    c.layout = ONNXB200_LAYOUT_NCHW;
+    c.epilogue = (bias ? ONNXB200_EPI_BIAS : 0) | (d->relu ? ONNXB200_EPI_RELU : 0);
+    c.precision = ONNXB200_PREC_DEFAULT;
+    return onnxb200_conv2d(h, &c, x, w, bias, nullptr, nullptr, nullptr, nullptr, nullptr, y);
+  }
+  Conv3dArgs a{};
+  a.N = (int)r.n;
+  a.C = (int)r.c;
+  a.CO = (int)r.co;
+  a.G = (int)r.g;
+  a.D = (int)r.in[0];
+  a.H = (int)r.in[1];
+  a.W = (int)r.in[2];
+  a.KD = (int)r.k[0];
+  a.KH = (int)r.k[1];
+  a.KW = (int)r.k[2];
+  a.OD = (int)r.out[0];
+  a.OH = (int)r.out[1];
+  a.OW = (int)r.out[2];
+  a.sd = (int)r.s[0];
+  a.sh = (int)r.s[1];
+  a.sw = (int)r.s[2];
+  a.pd = (int)r.pb[0];
+  a.ph = (int)r.pb[1];
+  a.pw = (int)r.pb[2];
+  a.dd = (int)r.dl[0];
+  a.dh = (int)r.dl[1];
+  a.dw = (int)r.dl[2];
+  a.relu = d->relu ? 1 : 0;
+  rc = conv3d_direct_launch(x, w, bias, y, a, h->stream);
+  h->launches++;
+  if (rc) return cuda_check(h, (cudaError_t)rc, "Conv3d launch");
+  return ONNXB200_OK;
+}
+
 int onnxb200_conv2d(onnxb200_handle* h, const onnxb200_conv_desc* d, const float* x,
                     const float* w, const float* bias, const float* bn_scale, const float* bn_bias,
                     const float* bn_mean, const float* bn_var, const float* residual, float* y) {

@@ -126,6 +126,16 @@ int add_broadcast_launch(const float* a, const float* b, float* y, int rank,
                          cudaStream_t stream);
 int relu_launch(const float* x, float* y, long long n, cudaStream_t stream);
 
+// 3-D direct convolution (NCDHW, fp32 on CUDA cores).
+struct Conv3dArgs {
+  int N, C, D, H, W, CO, G;
+  int KD, KH, KW, OD, OH, OW;
+  int sd, sh, sw, pd, ph, pw, dd, dh, dw;
+  int relu;
+};
+int conv3d_direct_launch(const float* x, const float* w, const float* bias, float* y, const Conv3dArgs& a,
+                         cudaStream_t stream);
+
 // Per-channel affine (BatchNormalization as scale/shift) over NHWC or NCHW.
 int channel_affine_launch(const float* x, const float* scale, const float* shift, float* y,
                           long long outer, int C, long long inner, int relu,

@@ -608,6 +608,57 @@ int add_broadcast_launch(const float* a, const float* b, float* y, int rank,
   return (int)cudaGetLastError();
 }
 
+// 3-D convolution, NCDHW in and out, weights [CO][C/group][KD][KH][KW]: one
+// thread per output element, fp32 fused multiply-adds over (ci, kd, kh, kw) in
+// that order, taps outside the input skipped (zero padding).  The reference's
+// compute_conv3d_direct_impl (src/ops/nn/conv.rs:937-1038) as a CUDA-core
+// kernel; consecutive threads take consecutive output columns.
+__global__ void conv3d_direct_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                     const float* __restrict__ bias, float* __restrict__ y, Conv3dArgs a) {
+  const long long total = (long long)a.N * a.CO * a.OD * a.OH * a.OW;
+  const int cg = a.C / a.G, cog = a.CO / a.G;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    long long r = i;
+    const int ow = (int)(r % a.OW); r /= a.OW;
+    const int oh = (int)(r % a.OH); r /= a.OH;
+    const int od = (int)(r % a.OD); r /= a.OD;
+    const int co = (int)(r % a.CO);
+    const int n = (int)(r / a.CO);
+    const int g = co / cog;
+    float acc = 0.f;
+    const float* wc = w + (long long)co * cg * a.KD * a.KH * a.KW;
+    for (int ci = 0; ci < cg; ++ci) {
+      const float* xc = x + ((long long)n * a.C + (long long)g * cg + ci) * a.D * a.H * a.W;
+      for (int kd = 0; kd < a.KD; ++kd) {
+        const int id = od * a.sd - a.pd + kd * a.dd;
+        if ((unsigned)id >= (unsigned)a.D) continue;
+        for (int kh = 0; kh < a.KH; ++kh) {
+          const int ih = oh * a.sh - a.ph + kh * a.dh;
+          if ((unsigned)ih >= (unsigned)a.H) continue;
+          const float* xr = xc + ((long long)id * a.H + ih) * a.W;
+          const float* wr = wc + ((long long)(ci * a.KD + kd) * a.KH + kh) * a.KW;
+          for (int kw = 0; kw < a.KW; ++kw) {
+            const int iw = ow * a.sw - a.pw + kw * a.dw;
+            if ((unsigned)iw < (unsigned)a.W) acc = fmaf(xr[iw], wr[kw], acc);
+          }
+        }
+      }
+    }
+    if (bias) acc += bias[co];
+    if (a.relu) acc = acc > 0.f ? acc : 0.f;
+    y[i] = acc;
+  }
+}
+
+int conv3d_direct_launch(const float* x, const float* w, const float* bias, float* y, const Conv3dArgs& a,
+                         cudaStream_t st) {
+  const long long total = (long long)a.N * a.CO * a.OD * a.OH * a.OW;
+  if (total == 0) return 0;
+  conv3d_direct_kernel<<<grid_for(total, kBlock), kBlock, 0, st>>>(x, w, bias, y, a);
+  return (int)cudaGetLastError();
+}
+
 // relu (src/ops/activations.rs:244-246): v > 0 ? v : 0 (NaN -> 0).
 __global__ void relu_kernel(const float* __restrict__ x, float* __restrict__ y, long long n) {
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;

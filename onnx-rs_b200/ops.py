@@ -21,7 +21,7 @@ from typing import Dict, List, Optional, Sequence
 import torch
 
 from . import _capi as C
-from .runtime import (Handle, InvalidOperator, ValidationError, dptr)
+from .runtime import (Handle, InvalidOperator, UnsupportedFeature, ValidationError, dptr)
 
 
 class ExecutionContext:
@@ -66,15 +66,18 @@ class Operator:
 
 # --------------------------------------------------------------------------- Conv
 class Conv(Operator):
-    """Conv (src/ops/nn/conv.rs:115-323), 2-D, with optional fused epilogue."""
+    """Conv (src/ops/nn/conv.rs:115-323): 2-D with an optional fused epilogue
+    (BatchNormalization, residual Add, Relu) on the tensor-core path; 1-D (NCL,
+    run as 2-D of height 1) and 3-D (NCDHW, CUDA cores) with bias and Relu.
+    strides / pads / dilations default per rank (ONNX: ones, zeros, ones)."""
     op_type = "Conv"
     min_inputs = 2
 
-    def __init__(self, strides=(1, 1), pads=(0, 0, 0, 0), dilations=(1, 1), group=1, auto_pad="NOTSET",
+    def __init__(self, strides=None, pads=None, dilations=None, group=1, auto_pad="NOTSET",
                  precision=None, relu=False):
-        self.strides = list(strides)
-        self.pads = list(pads)
-        self.dilations = list(dilations)
+        self.strides = None if strides is None else list(strides)
+        self.pads = None if pads is None else list(pads)
+        self.dilations = None if dilations is None else list(dilations)
         self.group = int(group)
         self.auto_pad = auto_pad
         self.precision = precision
@@ -83,8 +86,39 @@ class Conv(Operator):
     @classmethod
     def from_node(cls, node, **kw):
         a = _attrs(node)
-        return cls(a.get("strides", (1, 1)), a.get("pads", (0, 0, 0, 0)), a.get("dilations", (1, 1)),
-                   a.get("group", 1), a.get("auto_pad", "NOTSET"), **kw)
+        return cls(a.get("strides"), a.get("pads"), a.get("dilations"), a.get("group", 1),
+                   a.get("auto_pad", "NOTSET"), **kw)
+
+    def _attr(self, sp):
+        """strides, pads (begin..., end...), dilations for `sp` spatial dims."""
+        st = self.strides if self.strides is not None else [1] * sp
+        pd = self.pads if self.pads is not None else [0] * (2 * sp)
+        dl = self.dilations if self.dilations is not None else [1] * sp
+        if len(st) != sp or len(pd) != 2 * sp or len(dl) != sp:
+            raise ValidationError(C.ERR_VALIDATION, f"Conv: attributes do not match {sp} spatial dims")
+        return st, pd, dl
+
+    def nd_desc(self, x_shape, w_shape):
+        """onnxb200_conv_nd_desc for a 1-D, 2-D or 3-D input."""
+        sp = len(x_shape) - 2
+        if sp < 1 or sp > 3 or len(w_shape) != len(x_shape):
+            raise ValidationError(C.ERR_VALIDATION, "Conv supports only 1D, 2D, and 3D convolutions")
+        st, pd, dl = self._attr(sp)
+        d = C.ConvNdDesc()
+        d.spatial = sp
+        d.n, d.c = x_shape[0], x_shape[1]
+        d.c_out = w_shape[0]
+        d.group = self.group
+        for i in range(sp):
+            d.in_[i] = x_shape[2 + i]
+            d.kernel[i] = w_shape[2 + i]
+            d.stride[i] = st[i]
+            d.pad_begin[i] = pd[i]
+            d.pad_end[i] = pd[sp + i]
+            d.dilation[i] = dl[i]
+        d.auto_pad = C.AUTOPAD[self.auto_pad]
+        d.relu = 1 if self.relu else 0
+        return d
 
     def desc(self, x_shape, w_shape, layout=C.LAYOUT_NCHW, epilogue=0, prec=C.PREC_DEFAULT, eps=1e-5):
         d = C.ConvDesc()
@@ -93,9 +127,10 @@ class Conv(Operator):
         else:
             d.n, d.c, d.h, d.w = x_shape
         d.c_out, _, d.kh, d.kw = w_shape
-        d.stride_h, d.stride_w = self.strides
-        d.pad_top, d.pad_left, d.pad_bottom, d.pad_right = self.pads
-        d.dil_h, d.dil_w = self.dilations
+        st, pd, dl = self._attr(2)
+        d.stride_h, d.stride_w = st
+        d.pad_top, d.pad_left, d.pad_bottom, d.pad_right = pd
+        d.dil_h, d.dil_w = dl
         d.group = self.group
         d.auto_pad = C.AUTOPAD[self.auto_pad]
         d.layout = layout
@@ -105,6 +140,14 @@ class Conv(Operator):
         return d
 
     def output_shape(self, x_shape, w_shape) -> List[int]:
+        if len(x_shape) != 4:
+            d = self.nd_desc(x_shape, w_shape)
+            out = C.i64_array([0] * 5)
+            rank = ctypes.c_int()
+            rc = C.lib().onnxb200_conv_nd_output_shape(ctypes.byref(d), out, ctypes.byref(rank))
+            if rc != 0:
+                raise ValidationError(rc, "Conv: invalid shapes or attributes")
+            return [int(v) for v in out[:rank.value]]
         d = self.desc(x_shape, w_shape)
         out = C.i64_array([0] * 4)
         rc = C.lib().onnxb200_conv2d_output_shape(ctypes.byref(d), out)
@@ -125,6 +168,14 @@ class Conv(Operator):
         x, w = inputs[0], inputs[1]
         b = inputs[2] if len(inputs) > 2 else None
         h = ctx.handle
+        if x.dim() != 4:  # 1-D / 3-D: bias and Relu only
+            if bn is not None or residual is not None or layout != C.LAYOUT_NCHW:
+                raise UnsupportedFeature(C.ERR_UNSUPPORTED, "Conv: fused BN / residual / NHWC are 2-D only")
+            y = torch.empty(self.output_shape(tuple(x.shape), tuple(w.shape)), dtype=torch.float32,
+                            device=x.device)
+            d = self.nd_desc(tuple(x.shape), tuple(w.shape))
+            h.check(C.lib().onnxb200_conv_nd(h.ptr, ctypes.byref(d), dptr(x), dptr(w), dptr(b), dptr(y)), "Conv")
+            return [y]
         epi = (C.EPI_BIAS if b is not None else 0) | (C.EPI_BN if bn is not None else 0) | \
               (C.EPI_RESIDUAL if residual is not None else 0) | (C.EPI_RELU if self.relu else 0)
         eps = bn[4] if bn is not None else 1e-5

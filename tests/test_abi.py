@@ -74,6 +74,48 @@ def test_conv_output_shape_matches_oracle(ob, oracle, cfg):
     assert shape == exp
 
 
+@pytest.mark.parametrize("cfg", [
+    # x shape, w shape, strides, pads, dilations, group, auto_pad
+    ((1, 1, 5), (1, 1, 3), None, None, None, 1, "NOTSET"),
+    ((2, 4, 17), (6, 2, 5), (2,), (2, 1), (1,), 2, "NOTSET"),
+    ((2, 3, 16), (8, 3, 4), (3,), None, (2,), 1, "SAME_UPPER"),
+    ((1, 2, 9), (4, 2, 3), (2,), None, None, 1, "SAME_LOWER"),
+    ((1, 1, 2, 2, 2), (1, 1, 2, 2, 2), None, None, None, 1, "NOTSET"),
+    ((2, 4, 7, 9, 8), (6, 2, 3, 3, 2), (2, 1, 2), (1, 0, 1, 1, 2, 0), (1, 2, 1), 2, "NOTSET"),
+    ((1, 3, 8, 8, 8), (5, 3, 3, 3, 3), (2, 2, 2), None, None, 1, "SAME_UPPER"),
+])
+def test_conv_nd_output_shape_matches_oracle(ob, oracle, cfg):
+    """1-D and 3-D Conv::output_shapes (conv.rs:205-323) against the oracle's
+    shape rules (the oracle evaluates the same convolution directly)."""
+    xs, ws, st, pd, dl, g, ap = cfg
+    sp = len(xs) - 2
+    shape = ob.Conv(st, pd, dl, g, ap).output_shape(xs, ws)
+    st = st or [1] * sp
+    dl = dl or [1] * sp
+    if ap in ("SAME_UPPER", "SAME_LOWER"):
+        ps = [oracle.same_pads(xs[2 + i], ws[2 + i], st[i], dl[i], ap == "SAME_UPPER") for i in range(sp)]
+        pb, pe = [p[0] for p in ps], [p[1] for p in ps]
+    else:
+        pd = pd or [0] * (2 * sp)
+        pb, pe = pd[:sp], pd[sp:]
+    exp = [xs[0], ws[0]] + [oracle.conv_out_dim(xs[2 + i], ws[2 + i], st[i], pb[i], pe[i], dl[i])
+                            for i in range(sp)]
+    assert shape == exp
+    if ap == "NOTSET":  # the oracle's direct convolution produces that shape
+        x = np.zeros(xs, np.float32)
+        w = np.zeros(ws, np.float32)
+        assert list(oracle.conv_nd_direct(x, w, None, st, pb + pe, dl, g).shape) == exp
+
+
+def test_conv_nd_rejects_bad_attributes(ob):
+    with pytest.raises(ob.ValidationError):
+        ob.Conv((1, 1), None, None).output_shape((1, 2, 8), (3, 2, 3))  # 2 strides for 1 spatial dim
+    with pytest.raises(ob.ValidationError):
+        ob.Conv().output_shape((1, 2, 2, 2, 2, 2), (1, 2, 1, 1, 1, 1))  # 4 spatial dims
+    with pytest.raises(ob.ValidationError):
+        ob.Conv(group=3).output_shape((1, 8, 5), (4, 2, 3))
+
+
 def test_conv_output_shape_rejects_bad_groups(ob):
     with pytest.raises(ob.ValidationError):
         ob.Conv(group=3).output_shape((1, 8, 5, 5), (4, 2, 3, 3))

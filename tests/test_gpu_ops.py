@@ -75,6 +75,57 @@ def test_conv_small(ob, oracle, ctx, case, precision):
     assert_close(y, ref, rtol, atol, f"{name}/{precision}")
 
 
+@pytest.mark.parametrize("name", ["conv1d", "conv3d"])
+def test_conv_nd_known_answers(ob, ctx, name):
+    """The reference's 1-D / 3-D known answers (conv.rs:1487-1529, 1594-1631),
+    exact as the reference asserts (small integers are exact in every path)."""
+    import json, os
+    case = next(c for c in json.load(open(os.path.join(os.path.dirname(__file__), "golden",
+                                                         "reference_known_answers.json")))["cases"]
+                if c["name"] == name)
+    conv = ob.Conv(case["strides"], case["pads"], case["dilations"], case["group"])
+    y = np_(conv.compute([cu(case["x"]), cu(case["w"])], ctx)[0])
+    assert list(y.shape) == case["expected_shape"]
+    np.testing.assert_array_equal(y, np.array(case["expected"], np.float32))
+
+
+CONV_ND = [
+    # name, x shape, co, kernel, strides, pads (begin..., end...), dilations, group, auto_pad
+    ("1d_plain", (2, 16, 50), 24, (5,), (1,), (2, 2), (1,), 1, "NOTSET"),
+    ("1d_s2_dil2", (3, 8, 61), 16, (3,), (2,), (1, 3), (2,), 1, "NOTSET"),
+    ("1d_grouped", (2, 32, 40), 32, (3,), (1,), (1, 1), (1,), 4, "NOTSET"),
+    ("1d_same_upper", (1, 12, 33), 20, (4,), (3,), None, (1,), 1, "SAME_UPPER"),
+    ("1d_wide_k", (4, 64, 128), 64, (9,), (1,), (4, 4), (1,), 1, "NOTSET"),
+    ("3d_plain", (2, 4, 6, 7, 8), 8, (3, 3, 3), (1, 1, 1), (1, 1, 1, 1, 1, 1), (1, 1, 1), 1, "NOTSET"),
+    ("3d_strided", (1, 3, 9, 10, 11), 6, (3, 2, 3), (2, 1, 2), (1, 0, 1, 1, 1, 0), (1, 2, 1), 1, "NOTSET"),
+    ("3d_grouped", (2, 8, 5, 6, 7), 12, (2, 3, 3), (1, 1, 1), (0, 1, 1, 1, 1, 1), (1, 1, 1), 4, "NOTSET"),
+    ("3d_same_lower", (1, 5, 7, 7, 7), 4, (3, 3, 3), (2, 2, 2), None, (1, 1, 1), 1, "SAME_LOWER"),
+]
+
+
+@pytest.mark.parametrize("case", CONV_ND, ids=lambda c: c[0])
+def test_conv_nd(ob, oracle, ctx, case):
+    """1-D (tensor cores, 3xTF32) and 3-D (CUDA cores, fp32) Conv + bias + Relu
+    against the oracle's direct N-d convolution (compute_conv_direct, conv.rs:609-706)."""
+    name, xs, co, k, st, pd, dl, g, ap = case
+    rng = np.random.default_rng(12)
+    x = rng.standard_normal(xs).astype(np.float32)
+    ws = (co, xs[1] // g) + tuple(k)
+    w = (rng.standard_normal(ws) * np.sqrt(2.0 / np.prod(ws[1:]))).astype(np.float32)
+    b = rng.uniform(-0.1, 0.1, co).astype(np.float32)
+    conv = ob.Conv(st, pd, dl, g, ap, precision="3xtf32", relu=True)
+    y = np_(conv.compute([cu(x), cu(w), cu(b)], ctx)[0])
+    sp = len(xs) - 2
+    if ap in ("SAME_UPPER", "SAME_LOWER"):
+        ps = [oracle.same_pads(xs[2 + i], k[i], st[i], dl[i], ap == "SAME_UPPER") for i in range(sp)]
+        pads = [p[0] for p in ps] + [p[1] for p in ps]
+    else:
+        pads = list(pd)
+    ref = oracle.relu(oracle.conv_nd_direct(x, w, b, list(st), pads, list(dl), g))
+    assert y.shape == ref.shape
+    assert_close(y, ref, 1e-5, 1e-4, name)
+
+
 def test_conv_stem_config(ob, oracle, ctx, handle):
     """Single Conv+Relu graph (stem 7x7/2, seed 0) through Conv::compute, 3xTF32."""
     nodes, inits, ins, outs = ob.workloads.stem_conv(0)
