@@ -235,7 +235,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int OHW = p.OH * p.OW;
         for (int item = warp - kLoadWarp0; item < total_items; item += NL) {
           const int s = item % S1;
-          if (!mbar_wait(s1_empty(s), ((item / S1) & 1) ^ 1, abort_flag, p.status)) break;
+          // Every coordinate of this item's loads is worked out before waiting
+          // for its stage: the integer divisions take ~2k cycles, which would
+          // otherwise sit between the stage's release and its refill, i.e. on
+          // the round trip that bounds the K loop.
           const int tj = item / p.num_kb;
           const int kb = item - tj * p.num_kb;
           int b, mt, nt;
@@ -246,27 +249,39 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int a_taps = p.a_mode == kALoadIm2colTaps ? max(0, min(kBK / p.Cs, (p.K - k0) / p.Cs))
                                                           : (k0 < p.K ? 1 : 0);
           const uint32_t a_box = p.a_mode == kALoadIm2colTaps ? kBM * p.Cs * 4 : L::kARaw;
-          mbar_arrive_expect_tx(s1_full(s), a_taps * a_box + (L::kSplit ? 2 : 1) * L::kBBytes);
+          const uint32_t tx_bytes = a_taps * a_box + (L::kSplit ? 2 : 1) * L::kBBytes;
           const int tap = k0 / p.Cs;
           const int c0 = k0 - tap * p.Cs;
           const uint32_t dst = a_raw + s * L::kARaw;
+          int a_r0 = 0, a_x = 0, a_y = 0, a_n = 0;
+          uint16_t off_w[kBK / 4], off_h[kBK / 4];  // im2col tap offsets (<= 8 taps per k-block)
           if (p.a_mode == kALoadTma2d) {
-            const int row0 = (p.a_off ? (int)(p.a_off[b] / p.Cs) : 0) + mt * kBM;
-            if (a_taps) tma_load_2d(dst, &tm_a, c0, row0, s1_full(s));
+            a_r0 = (p.a_off ? (int)(p.a_off[b] / p.Cs) : 0) + mt * kBM;
           } else {
             const int m0 = mt * kBM;
-            const int n0 = m0 / OHW;
-            const int rem = m0 - n0 * OHW;
+            a_n = m0 / OHW;
+            const int rem = m0 - a_n * OHW;
             const int oh0 = rem / p.OW;
-            const int ow0 = rem - oh0 * p.OW;
-            for (int j = 0; j < a_taps; ++j) {
+            a_x = (rem - oh0 * p.OW) * p.sw - p.pw;
+            a_y = oh0 * p.sh - p.ph;
+#pragma unroll
+            for (int j = 0; j < kBK / 4; ++j) {
               const int r = (tap + j) / p.KW;
-              const int q = tap + j - r * p.KW;
-              tma_load_im2col_4d(dst + j * a_box, &tm_a, c0, ow0 * p.sw - p.pw, oh0 * p.sh - p.ph, n0,
-                                 (uint16_t)(q * p.dw), (uint16_t)(r * p.dh), s1_full(s));
+              off_w[j] = (uint16_t)((tap + j - r * p.KW) * p.dw);
+              off_h[j] = (uint16_t)(r * p.dh);
             }
           }
           const int brow = nt * BN + (p.b_row ? p.b_row[b] : 0);
+          if (!mbar_wait(s1_empty(s), ((item / S1) & 1) ^ 1, abort_flag, p.status)) break;
+          mbar_arrive_expect_tx(s1_full(s), tx_bytes);
+          if (p.a_mode == kALoadTma2d) {
+            if (a_taps) tma_load_2d(dst, &tm_a, c0, a_r0, s1_full(s));
+          } else {
+#pragma unroll
+            for (int j = 0; j < kBK / 4; ++j)
+              if (j < a_taps)
+                tma_load_im2col_4d(dst + j * a_box, &tm_a, c0, a_x, a_y, a_n, off_w[j], off_h[j], s1_full(s));
+          }
           tma_load_2d(b_hi + s * L::kBStride, &tm_hi, k0, brow, s1_full(s));
           if (L::kSplit) tma_load_2d(b_lo + s * L::kBStride, &tm_lo, k0, brow, s1_full(s));
         }
