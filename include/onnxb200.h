@@ -109,6 +109,16 @@ ONNXB200_API int onnxb200_synchronize(onnxb200_handle* h);
 ONNXB200_API int64_t onnxb200_kernel_launches(const onnxb200_handle* h);
 /* Number of SMs of the handle's device. */
 ONNXB200_API int onnxb200_num_sms(const onnxb200_handle* h);
+/* Device memory on the handle's GPU, for bindings without a CUDA runtime of
+ * their own (the reference's operators take host tensors: copy in, compute,
+ * copy out).  Copies are asynchronous on the handle's stream (synchronize
+ * before reading a device-to-host copy's destination). */
+#define ONNXB200_COPY_H2D 0
+#define ONNXB200_COPY_D2H 1
+#define ONNXB200_COPY_D2D 2
+ONNXB200_API int onnxb200_malloc(onnxb200_handle* h, size_t bytes, void** ptr);
+ONNXB200_API int onnxb200_free(onnxb200_handle* h, void* ptr);
+ONNXB200_API int onnxb200_memcpy(onnxb200_handle* h, void* dst, const void* src, size_t bytes, int kind);
 
 /* ---------------------------------------------------------------- Conv */
 typedef struct onnxb200_conv_desc {

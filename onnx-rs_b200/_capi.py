@@ -124,6 +124,9 @@ SIGNATURES = {
     "onnxb200_synchronize": (_int, [_vp]),
     "onnxb200_kernel_launches": (_i64, [_vp]),
     "onnxb200_num_sms": (_int, [_vp]),
+    "onnxb200_malloc": (_int, [_vp, ctypes.c_size_t, ctypes.POINTER(_vp)]),
+    "onnxb200_free": (_int, [_vp, _vp]),
+    "onnxb200_memcpy": (_int, [_vp, _vp, _vp, ctypes.c_size_t, _int]),
     "onnxb200_conv2d_output_shape": (_int, [ctypes.POINTER(ConvDesc), _i64p]),
     "onnxb200_conv2d": (_int, [_vp, ctypes.POINTER(ConvDesc)] + [_vp] * 9),
     "onnxb200_conv_plan_create": (_int, [_vp, ctypes.POINTER(ConvDesc)] + [_vp] * 6 + [ctypes.POINTER(_vp)]),

@@ -504,6 +504,36 @@ void* onnxb200_get_stream(onnxb200_handle* h) { return h ? (void*)h->stream : nu
 
 int64_t onnxb200_kernel_launches(const onnxb200_handle* h) { return h ? h->launches : -1; }
 
+int onnxb200_malloc(onnxb200_handle* h, size_t bytes, void** ptr) {
+  if (!h || !ptr) return ONNXB200_ERR_INVALID_ARGUMENT;
+  *ptr = nullptr;
+  cudaSetDevice(h->device);
+  if (bytes == 0) return ONNXB200_OK;
+  cudaError_t e = cudaMalloc(ptr, bytes);
+  if (e != cudaSuccess) {
+    *ptr = nullptr;
+    return cuda_check(h, e, "device allocation");
+  }
+  return ONNXB200_OK;
+}
+
+int onnxb200_free(onnxb200_handle* h, void* ptr) {
+  if (!h) return ONNXB200_ERR_INVALID_ARGUMENT;
+  if (!ptr) return ONNXB200_OK;
+  cudaSetDevice(h->device);
+  return cuda_check(h, cudaFree(ptr), "device free");
+}
+
+int onnxb200_memcpy(onnxb200_handle* h, void* dst, const void* src, size_t bytes, int kind) {
+  if (!h || (bytes && (!dst || !src)) || kind < 0 || kind > 2) return ONNXB200_ERR_INVALID_ARGUMENT;
+  if (bytes == 0) return ONNXB200_OK;
+  cudaSetDevice(h->device);
+  const cudaMemcpyKind k = kind == ONNXB200_COPY_H2D   ? cudaMemcpyHostToDevice
+                           : kind == ONNXB200_COPY_D2H ? cudaMemcpyDeviceToHost
+                                                       : cudaMemcpyDeviceToDevice;
+  return cuda_check(h, cudaMemcpyAsync(dst, src, bytes, k, h->stream), "copy");
+}
+
 int onnxb200_num_sms(const onnxb200_handle* h) { return h ? h->num_sms : -1; }
 
 int onnxb200_synchronize(onnxb200_handle* h) {
