@@ -20,11 +20,14 @@ constexpr int kBM = 128;
 int igemm_pick_bn(const IgemmParams& p, int precision, int num_sms) {
   const int nc = p.Nc;
   if (nc <= 64) return 64;
+  // Small problems (e.g. the late layers of a 32-image batch): 64-column tiles
+  // when twice as many tiles still fit in one wave, so that more SMs work.
+  const long long mt = (long long)((p.M + kBM - 1) / kBM) * p.batches;
+  if (2 * mt * ((nc + 127) / 128) <= num_sms) return 64;
   // 3xTF32 (chunked accumulators, 3 x BN columns) and BF16 keep A slots in TMEM
   // next to the accumulators: at most 128 columns wide.  TF32 keeps only two
   // whole-tile accumulators, so 256 fits the 512 TMEM columns.
   if (precision == kPrec3xTF32 || precision == kPrecBF16) return 128;
-  const long long mt = (long long)((p.M + kBM - 1) / kBM) * p.batches;
   // Wide tiles halve A re-reads; use them when there are enough tiles to fill the GPU.
   if (nc >= 256 && mt * ((nc + 255) / 256) >= 2ll * num_sms) return 256;
   return 128;
