@@ -14,11 +14,13 @@
 //               Relu.  Warp w stores (and loads the residual of) its own 32 rows of
 //               each 16- or 32-column group with its own TMA boxes (the hardware
 //               clips rows >= M and columns >= N).
-//   warps 4-7   A loaders.  TMA modes: one thread issues, per k-block, the A tile
-//               (2-D tile of the [pixels][channels] matrix for 1x1 stride-1 convs and
-//               GEMMs, or an im2col box for k x k convs: the hardware walks 128 output
-//               pixels across rows and images, zero fill = padding) and the weight
-//               tiles.  Taps mode (4, 8 or 16 channels): one im2col box per filter
+//   warps 4-7   loaders.  TMA modes: lane 0 of each warp takes every fourth
+//               k-block (a TMA issue holds its thread for hundreds of cycles) and
+//               issues its A tile (2-D tile of the [pixels][channels] matrix for 1x1
+//               stride-1 convs and GEMMs, or an im2col box for k x k convs: the
+//               hardware walks 128 output pixels across rows and images, zero fill =
+//               padding) and its weight tiles, coordinates worked out before the
+//               wait for the stage.  Taps mode (4, 8 or 16 channels): one im2col box per filter
 //               tap.  Gather mode (other channel counts): 16-byte cp.async copies
 //               with zero fill.
 //   warps 8-11  converters: warp 8+q owns TMEM lanes 32q..32q+31 (= tile rows).
@@ -28,7 +30,10 @@
 //               bits), which is only rewritten for taps-mode boxes or K padding.
 //   warp 12     TMEM allocation and one thread issuing tcgen05.mma (kind::tf32 or
 //               kind::f16), A from TMEM (from shared memory in TF32), B from shared
-//               memory; this thread's issue rate bounds the kernel.
+//               memory.
+// The K loop is bound by the number of operand stages in flight: a stage's round
+// trip (release -> TMA issue -> landing -> conversion -> MMAs -> commit) takes
+// ~5k cycles, of which the TMA issue is ~2k.
 // 3xTF32: a*b ~= a_hi*b_hi + a_hi*b_lo + a_lo*b_hi (Ootomo & Yokota, 2022), with the
 // same split for both operands.  With BN = 64 the B hi and lo rows are stacked so
 // that one N = 128 MMA computes two of the three products.  The tensor core adds

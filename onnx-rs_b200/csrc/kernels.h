@@ -64,7 +64,8 @@ int igemm_pick_bn(const IgemmParams& p, int precision, int num_sms);
 int igemm_launch(const IgemmParams& p, const CUtensorMap& tm_hi, const CUtensorMap& tm_lo,
                  const CUtensorMap& tm_a, int precision, int bn, int num_sms, cudaStream_t stream);
 
-// The fp32-input kernel (3xTF32 / TF32, k-blocks of 16) behind igemm_launch.
+// The tcgen05 kernel (3xTF32 / TF32 / BF16 operands from fp32 activations,
+// k-blocks of 32) behind igemm_launch.
 int igemm3_launch(const IgemmParams& p, const CUtensorMap& tm_hi, const CUtensorMap& tm_lo,
                   const CUtensorMap& tm_a, int precision, int bn, int num_sms, cudaStream_t stream);
 
