@@ -44,6 +44,17 @@ def test_null_arguments_rejected(ob):
     assert lib.onnxb200_destroy(None) == ob._capi.ERR_INVALID_ARGUMENT
     assert lib.onnxb200_synchronize(None) == ob._capi.ERR_INVALID_ARGUMENT
     assert lib.onnxb200_graph_destroy(None) == ob._capi.ERR_INVALID_ARGUMENT
+    assert lib.onnxb200_graph_run_host_pipelined(None, None, 1, None, None) == ob._capi.ERR_INVALID_ARGUMENT
+    assert lib.onnxb200_graph_build_from_model(None, None, None, 0, None) == ob._capi.ERR_INVALID_ARGUMENT
+    assert lib.onnxb200_conv_nd(None, None, None, None, None, None) == ob._capi.ERR_INVALID_ARGUMENT
+    p = ctypes.c_void_p()
+    assert lib.onnxb200_malloc(None, 16, ctypes.byref(p)) == ob._capi.ERR_INVALID_ARGUMENT
+    assert lib.onnxb200_free(None, None) == ob._capi.ERR_INVALID_ARGUMENT
+    assert lib.onnxb200_memcpy(None, None, None, 16, 0) == ob._capi.ERR_INVALID_ARGUMENT
+    assert lib.onnxb200_model_parse(None, 0, None, None, None, 0) == ob._capi.ERR_INVALID_ARGUMENT
+    assert lib.onnxb200_model_load(None, None, None, 0) == ob._capi.ERR_INVALID_ARGUMENT
+    assert lib.onnxb200_model_destroy(None) == ob._capi.OK
+    assert lib.onnxb200_status_string(ob._capi.ERR_PROTOBUF) == b"protobuf parsing error"
 
 
 @pytest.mark.parametrize("cfg", [
