@@ -15,7 +15,11 @@ Prints ONE JSON line (rank 0):
              (e2e.unpipelined_value: onnxb200_graph_run_host one step at a time)
   roofline   the tcgen05 implicit-GEMM kernel (all Conv/Gemm steps of one run):
              algorithmic FLOPs / device time of those steps, against the
-             effective 3xTF32 peak = measured dense bf16 / 6
+             effective 3xTF32 peak = measured dense bf16 / 6 (burst; the
+             sustained fraction beside it), plus achieved GB/s of the
+             memory-bound steps
+  fast_modes the same workload in the 1xTF32 and BF16 fast modes, each with its
+             own roofline
   cpu_baseline  the oracle (a C restatement of the reference's CPU operators,
              batch-parallel like the reference's rayon use) on a bounded sample
 `--impl reference` times that same CPU path alone (rank 0), as the reference arm.
@@ -40,8 +44,8 @@ METRIC_FAST = {"tf32": "ResNet-50 v1.5 images/sec (batch 256, fast mode: 1xTF32)
                "bf16": "ResNet-50 v1.5 images/sec (batch 256, fast mode: BF16)",
                "fp32": "ResNet-50 v1.5 images/sec (batch 256, fp32 on CUDA cores)"}
 # DRAM bytes per igemm_tc3_kernel launch, mean over the 54 launches of one
-# batch-256 3xTF32 run: ncu dram__bytes_read.sum + dram__bytes_write.sum
-# (profiles/resnet50_b256_launch_list.md).
+# batch-256 3xTF32 run: dram__bytes_read.sum + dram__bytes_write.sum from an
+# ncu DRAM capture of this workload (a measured constant, not re-derived here).
 TRAFFIC_PER_LAUNCH_3XTF32 = 467.5e6
 L2_BYTES = 126 * 1024 * 1024
 
@@ -107,56 +111,77 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(rows)}
 
 
+class OracleResNet50:
+    """The oracle's ResNet-50 v1.5 (a C restatement of the reference's CPU
+    operators, batch-parallel like the reference's rayon use) on a bounded
+    sample batch: every host thread this process may use (at most 64, so that
+    the sample's activations stay a few GB), one image per thread."""
+
+    def __init__(self, images=None):
+        import importlib
+        from oracle import oracle as orc
+        ob = importlib.import_module("onnx-rs_b200")
+        orc.build()
+        try:
+            self.avail = len(os.sched_getaffinity(0))
+        except AttributeError:
+            self.avail = os.cpu_count() or 1
+        self.threads = max(1, min(self.avail, 64))
+        self.n = images or self.threads
+        self.orc = orc
+        self.nodes, self.inits, _, self.outs = ob.workloads.resnet50(batch=self.n, seed=SEED)
+        self.x = ob.workloads.resnet_input(SEED, self.n)
+
+    def run(self):
+        """One pass over the sample; returns its wall time in seconds."""
+        t0 = time.perf_counter()
+        self.orc.run_graph(self.nodes, self.inits, {"X": self.x}, self.outs, nthreads=self.threads)
+        return time.perf_counter() - t0
+
+    def sample(self, runs, t):
+        return (f"ResNet-50 v1.5 batch {self.n} (a sample of the batch-256 workload), seed {SEED}, oracle C "
+                f"restatement of the reference's CPU operators (im2col+GEMM / direct conv), batch split over "
+                f"{self.threads} of {self.avail} available host threads, median of {runs} run(s), {t:.2f} s each")
+
+
 def cpu_baseline(steps=1, images=None, min_seconds=0.0, max_steps=8):
-    """Oracle ResNet-50 (3xTF32 path's reference semantics, fp32) on host cores:
-    every host thread this process may use (at most 64, so that the sample's
-    activations stay a few GB), one image per thread; at least `steps` runs and
-    more (up to `max_steps`) until `min_seconds` of work have been timed."""
-    import importlib
-    from oracle import oracle as orc
-    ob = importlib.import_module("onnx-rs_b200")
-    orc.build()
-    try:
-        avail = len(os.sched_getaffinity(0))
-    except AttributeError:
-        avail = os.cpu_count() or 1
-    threads = max(1, min(avail, 64))
-    n = images or threads
-    nodes, inits, ins, outs = ob.workloads.resnet50(batch=n, seed=SEED)
-    x = ob.workloads.resnet_input(SEED, n)
+    """The oracle on host cores: at least `steps` runs and more (up to
+    `max_steps`) until `min_seconds` of work have been timed."""
+    o = OracleResNet50(images)
     times = []
     while len(times) < steps or (sum(times) < min_seconds and len(times) < max_steps):
-        t0 = time.perf_counter()
-        orc.run_graph(nodes, inits, {"X": x}, outs, nthreads=threads)
-        times.append(time.perf_counter() - t0)
+        times.append(o.run())
     t = statistics.median(times)
-    return {"value": n / t, "unit": "images/s", "cores": threads, "kind": "port",
-            "sample": f"ResNet-50 v1.5 batch {n} (of 256), seed {SEED}, oracle C restatement of the reference's "
-                      f"CPU operators (im2col+GEMM / direct conv, batch split over {threads} of {avail} "
-                      f"available host threads), median of {len(times)} run(s), {t:.2f} s each"}
+    return {"value": o.n / t, "unit": "images/s", "cores": o.threads, "kind": "port",
+            "sample": o.sample(len(times), t)}
 
 
 def run_reference(args):
+    """The reference arm: the reference's CPU algorithms (the oracle's C
+    restatement; the reference itself is Rust and cannot be built here) on the
+    host cores.  A step is one pass over the sample batch (one image per host
+    thread); the line reports that batch and the measured per-pass time."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    res = None
-    times = []
-    for i in range(args.warmup + args.steps):
-        r = cpu_baseline(steps=1)
-        if i >= args.warmup:
-            times.append(r)
-        res = r
-    vals = [r["value"] for r in times]
-    value = statistics.median(vals)
-    ms = 1000.0 * GLOBAL_BATCH / value
+    o = OracleResNet50()
+    for _ in range(args.warmup):
+        o.run()
+    times = [o.run() for _ in range(args.steps)]
+    t = statistics.median(times)
+    value = o.n / t
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "images/s",
-            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * t,
+            "ms_per_step_mean": 1000.0 * sum(times) / len(times),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "config": {"workload": "resnet50_v1.5_b256", "global_batch": GLOBAL_BATCH,
-                                            "seq_len": None, "parallelism": "cpu threads over batch"},
-            "cpu_baseline": {"value": value, "unit": "images/s", "cores": res["cores"], "kind": res["kind"],
-                             "sample": res["sample"]},
+            "data": "synthetic",
+            "config": {"workload": "resnet50_v1.5_b256", "global_batch": o.n, "per_step_batch": o.n,
+                       "sample": f"each step is one pass over a batch-{o.n} sample of the batch-"
+                                 f"{GLOBAL_BATCH} workload (same seed, same images 0..{o.n - 1})",
+                       "full_workload_batch": GLOBAL_BATCH,
+                       "seq_len": None, "parallelism": f"cpu: {o.threads} threads over the batch"},
+            "cpu_baseline": {"value": value, "unit": "images/s", "cores": o.threads, "kind": "port",
+                             "sample": o.sample(len(times), t)},
             "e2e": {"value": value, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -194,8 +219,7 @@ def run_single_workload(args):
     ctx = ob.ExecutionContext(h)
     flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device="cuda")
     peaks, peak_src = load_peaks()
-    bf16 = peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
-    tpeak = {"3xtf32": bf16 / 6.0, "tf32": bf16 / 2.0, "bf16": bf16, "fp32": bf16 / 2.0}[args.precision]
+    tpeak, tpeak_sus = tensor_peaks(peaks, args.precision)
     wl = args.workload
     if wl.startswith("conv:") or wl == "stem":
         if wl == "stem":
@@ -252,7 +276,8 @@ def run_single_workload(args):
     line = {"metric": metric, "value": value, "unit": unit, "n_gpus": 1, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "precision": args.precision,
             "data": "synthetic", "config": {"workload": name, "l2": "flushed between timed steps"},
-            "roofline": {"tensor": {"achieved": tf, "peak": tpeak, "unit": "TFLOP/s", "frac": tf / tpeak},
+            "roofline": {"tensor": {"achieved": tf, "peak": tpeak, "unit": "TFLOP/s", "frac": tf / tpeak,
+                                    "peak_sustained": tpeak_sus, "frac_of_sustained": tf / tpeak_sus},
                          "hbm": None if bytes_ is None else
                          {"achieved": bytes_ / ms / 1e6, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                           "frac": bytes_ / ms / 1e6 / peaks["hbm_gbs"]},
@@ -260,6 +285,54 @@ def run_single_workload(args):
             "gpu_launches": None}
     print(json.dumps(line), flush=True)
     h.close()
+
+
+def tensor_peaks(peaks, precision):
+    """(burst, sustained) dense peaks in TFLOP/s for a precision: tf32 = bf16 / 2;
+    the 3xTF32 effective peak = tf32 / 3 (three tf32 MMAs per product)."""
+    burst = peaks.get("bf16_tflops")
+    sus = peaks.get("bf16_tflops_sustained", burst)
+    div = {"3xtf32": 6.0, "tf32": 2.0, "bf16": 1.0, "fp32": 2.0}[precision]
+    return burst / div, sus / div
+
+
+def roofline_of(prof, peaks, peak_src, precision, traffic=None):
+    """Roofline of the contraction kernel over one profiled run (per-step CUDA
+    events): algorithmic FLOPs / summed device time of the Conv/Gemm steps,
+    against the burst peak (the steps last milliseconds, not seconds) with the
+    sustained-peak fraction beside it; and achieved GB/s of the memory-bound
+    step kinds against the measured HBM copy bandwidth."""
+    tc = [p for p in prof if p["kind"] in ("conv_tc", "gemm")]
+    tc_ms = sum(p["ms"] for p in tc)
+    tc_flops = sum(p["flops"] for p in tc)
+    achieved = tc_flops / (tc_ms / 1e3) / 1e12 if tc_ms > 0 else 0.0
+    burst, sus = tensor_peaks(peaks, precision)
+    tf32_burst = peaks["bf16_tflops"] / 2.0
+    mem = {}
+    for kind in ("maxpool", "gap", "convert", "add", "relu", "affine", "conv_direct"):
+        ps = [p for p in prof if p["kind"] == kind]
+        ms = sum(p["ms"] for p in ps)
+        if not ps or ms <= 0:
+            continue
+        by = sum(p["bytes"] for p in ps)
+        mem[kind] = {"launches": len(ps), "ms": round(ms, 4), "bytes": by, "achieved_gbs": by / ms / 1e6,
+                     "frac_of_hbm": by / ms / 1e6 / peaks["hbm_gbs"]}
+    basis = {"3xtf32": "3xTF32 effective = dense bf16 / 6 (tf32 = bf16 / 2, three tf32 MMAs per product)",
+             "tf32": "tf32 dense = dense bf16 / 2", "bf16": "dense bf16",
+             "fp32": "fp32 CUDA cores, compared against tf32 dense"}[precision]
+    kernel = "igemm_tc3_kernel" if precision != "fp32" else "conv_direct_kernel"
+    return {"bound": "tensor", "achieved": achieved, "peak": burst, "unit": "TFLOP/s",
+            "frac": achieved / burst if burst else None,
+            "peak_sustained": sus, "frac_of_sustained": achieved / sus if sus else None,
+            "traffic": traffic,
+            "traffic_note": "DRAM bytes per contraction launch (mean over the run's launches) from one ncu "
+                            "DRAM capture of this workload" if traffic else None,
+            "kernel": kernel + " (all Conv/Gemm launches of one run)",
+            "launches": len(tc), "flops_per_launch": tc_flops / max(1, len(tc)),
+            "peak_source": f"{peak_src} ({'MEASURED_PEAKS.json' if peak_src == 'measured' else 'fallback'}): "
+                           f"{basis}; `peak` = burst (bf16_tflops), `peak_sustained` = bf16_tflops_sustained",
+            "frac_of_raw_tf32": achieved / tf32_burst if precision in ("3xtf32", "tf32") else None,
+            "memory_bound": mem}
 
 
 def main():
@@ -273,6 +346,7 @@ def main():
     ap.add_argument("--precision", default="3xtf32", choices=["3xtf32", "tf32", "bf16", "fp32"])
     ap.add_argument("--batch", type=int, default=GLOBAL_BATCH, help="global batch")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-fast-modes", action="store_true", help="skip the tf32 / bf16 lines of the headline")
     ap.add_argument("--profile-json", default=None, help="write the per-step profile here")
     args = ap.parse_args()
     if args.impl == "reference":
@@ -315,46 +389,56 @@ def main():
     xfull = ob.workloads.resnet_input(SEED, args.batch)
     xs = np.ascontiguousarray(xfull[lo:hi])
     del xfull
+    peaks, peak_src = load_peaks()
 
     # one dedicated stream: the library's kernels, the L2 flush and the CUDA
     # events all go on it
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
-    h = ob.Handle(local, precision=args.precision)
-    assert h.stream_ptr == stream.cuda_stream
-    g = ob.Graph(h, nodes, inits, ins, outs)
     xin = torch.from_numpy(xs).cuda()
-    yout = g.alloc_outputs(xin.device)
-
-    for _ in range(args.warmup):
-        g.run([xin], yout)
-    h.synchronize()
-    prof = g.profile([xin], yout)
-    h.synchronize()
-    stats = g.stats()
-
     flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device="cuda")
-    clocks = ClockSampler(local)
-    clocks.start()
-    time.sleep(0.5)  # let nvidia-smi start sampling before the timed region
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    barrier()
-    torch.cuda.synchronize()
-    l0 = h.launches
-    for i in range(args.steps):
-        flush.zero_()  # evict L2 between timed iterations (outside the events)
-        starts[i].record(stream)
-        g.run([xin], yout)
-        ends[i].record(stream)
-    torch.cuda.synchronize()
-    barrier()
-    launches = h.launches - l0
-    h.synchronize()
-    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    ms_local = sum(step_ms) / len(step_ms)
-    ms = max_over_ranks(ms_local)
-    clk = clocks.stop()
+
+    def measure(precision, clocks=None):
+        """Device time of K graph replays of this rank's slice: CUDA events
+        around each step on the launching stream, L2 evicted between steps
+        (outside the events), max over ranks.  Also the time from the barrier's
+        release to this rank's last completion event (L2 flushes included)."""
+        h = ob.Handle(local, precision=precision)
+        assert h.stream_ptr == stream.cuda_stream
+        g = ob.Graph(h, nodes, inits, ins, outs)
+        yout = g.alloc_outputs(xin.device)
+        for _ in range(args.warmup):
+            g.run([xin], yout)
+        h.synchronize()
+        prof = g.profile([xin], yout)
+        h.synchronize()
+        if clocks:
+            clocks.start()
+            time.sleep(0.5)  # let nvidia-smi start sampling before the timed region
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        t_rel = torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize()
+        t_rel.record(stream)
+        l0 = h.launches
+        for i in range(args.steps):
+            flush.zero_()  # evict L2 between timed iterations (outside the events)
+            starts[i].record(stream)
+            g.run([xin], yout)
+            ends[i].record(stream)
+        torch.cuda.synchronize()
+        launches = h.launches - l0
+        clk = clocks.stop() if clocks else None
+        step_ms = [a.elapsed_time(b) for a, b in zip(starts, ends)]
+        ms = max_over_ranks(sum(step_ms) / len(step_ms))
+        from_barrier_ms = max_over_ranks(t_rel.elapsed_time(ends[-1]))
+        return {"h": h, "g": g, "yout": yout, "prof": prof, "ms": ms, "launches": launches, "clocks": clk,
+                "from_barrier_ms": from_barrier_ms}
+
+    m = measure(args.precision, ClockSampler(local))
+    h, g, prof, ms = m["h"], m["g"], m["prof"], m["ms"]
+    stats = g.stats()
     value = args.batch / (ms / 1000.0)
 
     # ---- end to end through the public host-buffer API
@@ -393,12 +477,8 @@ def main():
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
     e2e_value = args.batch / (e2e_ms / 1000.0)
 
-    # ---- roofline of the tcgen05 kernel over one run (per-step CUDA events)
-    peaks, peak_src = load_peaks()
-    tc = [p for p in prof if p["kind"] in ("conv_tc", "gemm")]
-    tc_ms = sum(p["ms"] for p in tc)
-    tc_flops = sum(p["flops"] for p in tc)
-    achieved = tc_flops / (tc_ms / 1e3) / 1e12 if tc_ms > 0 else 0.0
+    traffic = TRAFFIC_PER_LAUNCH_3XTF32 if args.precision == "3xtf32" and args.batch == 256 else None
+    roofline = roofline_of(prof, peaks, peak_src, args.precision, traffic)
     by_kind = {}
     for p in prof:
         d = by_kind.setdefault(p["kind"], {"n": 0, "ms": 0.0, "flops": 0.0, "bytes": 0.0})
@@ -407,33 +487,22 @@ def main():
         d["flops"] += p["flops"]
         d["bytes"] += p["bytes"]
     prof_total = sum(p["ms"] for p in prof)
-    bf16 = peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
-    if args.precision == "3xtf32":
-        peak = bf16 / 6.0
-        basis = "3xTF32 effective = sustained dense bf16 / 6 (tf32 = bf16/2, three MMAs per product)"
-    elif args.precision == "tf32":
-        peak = bf16 / 2.0
-        basis = "tf32 dense = sustained dense bf16 / 2"
-    elif args.precision == "bf16":
-        peak = bf16
-        basis = "sustained dense bf16"
-    else:
-        peak = bf16 / 2.0
-        basis = "fp32 CUDA cores compared against tf32 dense"
-    n_tc_launch = len(tc)
-    roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                "frac": achieved / peak if peak else None,
-                "traffic": TRAFFIC_PER_LAUNCH_3XTF32 if args.precision == "3xtf32" and args.batch == 256 else None,
-                "traffic_note": "DRAM bytes per conv launch from one ncu capture of this workload"
-                                " (bytes, mean over the run's launches)",
-                "kernel": ("igemm_tc_kernel" if args.precision == "bf16" else "igemm_tc3_kernel")
-                + " (all Conv/Gemm launches of one run)",
-                "launches": n_tc_launch, "flops_per_launch": tc_flops / max(1, n_tc_launch),
-                "peak_source": f"{peak_src}: {basis}",
-                "frac_of_raw_tf32": (3 * achieved / (bf16 / 2.0)) if args.precision == "3xtf32" else None}
     if args.profile_json and rank == 0:
         with open(args.profile_json, "w") as f:
             json.dump({"steps": prof, "by_kind": by_kind, "stats": stats}, f, indent=1)
+    g.close()
+    h.close()
+
+    # ---- the fast modes, separately reported: same workload, same timing
+    fast = {}
+    if args.precision == "3xtf32" and not args.no_fast_modes:
+        for prec in ("tf32", "bf16"):
+            fm = measure(prec)
+            fast[prec] = {"metric": METRIC_FAST[prec], "value": args.batch / (fm["ms"] / 1000.0),
+                          "unit": "images/s", "ms_per_step": fm["ms"], "gpu_launches": int(fm["launches"]),
+                          "roofline": roofline_of(fm["prof"], peaks, peak_src, prec)}
+            fm["g"].close()
+            fm["h"].close()
 
     line = None
     if rank == 0:
@@ -450,22 +519,25 @@ def main():
                        "seq_len": None, "parallelism": f"dp{world} (batch split, weights replicated)",
                        "l2": "flushed between timed steps (2x L2 memset outside the events)",
                        "conv_gflop_per_image": conv_flops_img / 1e9},
+            "from_barrier": {"value": args.batch * args.steps / (m["from_barrier_ms"] / 1000.0),
+                             "unit": "images/s",
+                             "note": "all K steps from the host barrier's release to the last rank's last "
+                                     "completion event (CUDA events, max over ranks), L2 flushes included"},
             "e2e": {"value": e2e_value, "unit": "images/s", "h2d_bytes_per_step": int(xs.nbytes) * world,
                     "mode": "onnxb200_graph_run_host_pipelined over the timed steps (each step's input "
                             "copy overlaps the previous step's compute)",
                     "unpipelined_value": args.batch / (e2e_single_ms / 1000.0),
                     "d2h_bytes_per_step": int(hout.numel() * 4) * world},
-            "gpu_launches": int(launches),
+            "gpu_launches": int(m["launches"]),
             "kernels_per_step": stats["kernels_per_run"],
             "roofline": roofline,
+            "fast_modes": fast or None,
             "profile_ms_by_kind": {k: round(v["ms"], 3) for k, v in by_kind.items()},
             "profile_total_ms": prof_total,
-            "clocks": clk,
+            "clocks": m["clocks"],
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
-    g.close()
-    h.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -193,11 +193,14 @@ ONNXB200_API int onnxb200_conv_plan_destroy(onnxb200_conv_plan* p);
  * weights + epilogue vectors larger than that are rejected with
  * ONNXB200_ERR_RESOURCE_EXHAUSTED (every ResNet-18/50 convolution fits).
  * Runs on the current device and the given stream (NULL = legacy default
- * stream) and returns once y is written (bounded wait); device-side failures
- * are returned as status codes.  The first call on a device looks up the
- * array's device address (cudaGetSymbolAddress), so make that first call
- * before any stream capture.  All calls share the array: calls that overlap on
- * the GPU (e.g. issued concurrently from several host threads) race on it.
+ * stream) and blocks until y is written (bounded wait); device-side failures
+ * are returned as status codes.  Because it blocks, it returns
+ * ONNXB200_ERR_UNSUPPORTED on a stream that is being captured.  The first call
+ * on a device looks up the array's device address (cudaGetSymbolAddress).  All
+ * calls share the array: calls that overlap on the GPU (e.g. issued
+ * concurrently from several host threads) race on it.  If a call returns
+ * ONNXB200_ERR_TIMEOUT its kernels may still be running; the next call on the
+ * device first waits (bounded) for them before it reuses the array.
  * d->layout must be ONNXB200_LAYOUT_NHWC. */
 #define ONNXB200_NOALLOC_SCRATCH_BYTES (24u << 20)
 ONNXB200_API int onnxb200_conv2d_nhwc_noalloc(void* cuda_stream, const onnxb200_conv_desc* d,
@@ -332,6 +335,28 @@ ONNXB200_API int onnxb200_graph_run_host_pipelined(onnxb200_handle* h, onnxb200_
                                                    float* const* outputs);
 ONNXB200_API int onnxb200_graph_output_shape(const onnxb200_graph* g, int index, int64_t* shape,
                                              int* rank);
+
+/* Shape inference over a whole node list without building a graph: host only
+ * (no handle, no GPU, no device memory).  The planner's
+ * infer_node_output_shapes (src/memory/planner.rs:908-960), i.e.
+ * Operator::output_shapes (src/ops/registry.rs:14-27) applied node by node in
+ * topological order.  `known` gives the shapes of the initializers and graph
+ * inputs (their data is not read and may be NULL).  Fills shapes[0..max_shapes)
+ * with every node output, node by node in the given order (name points into
+ * `nodes`); *n_shapes receives the count, and ONNXB200_ERR_RESOURCE_EXHAUSTED
+ * is returned when it exceeds max_shapes.  Errors as onnxb200_graph_build
+ * (ValidationError for inconsistent shapes, InvalidOperator for an op that is
+ * not on this path, InvalidGraph for a cycle or a tensor without a producer);
+ * the message goes to err (may be NULL). */
+typedef struct onnxb200_shape_info {
+  const char* name;
+  int64_t dims[8];
+  int rank;
+} onnxb200_shape_info;
+ONNXB200_API int onnxb200_infer_shapes(const onnxb200_node* nodes, int n_nodes,
+                                       const onnxb200_tensor_info* known, int n_known,
+                                       onnxb200_shape_info* shapes, int max_shapes, int* n_shapes,
+                                       char* err, size_t err_len);
 
 /* Per-step profile of one eager run: the device-side counterpart of the
  * reference's per-node profiling events (src/execution/engine.rs:549-649,

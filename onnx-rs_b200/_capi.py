@@ -105,6 +105,10 @@ class ModelInfo(ctypes.Structure):
                 ("producer_name", ctypes.c_char_p), ("graph_name", ctypes.c_char_p)]
 
 
+class ShapeInfo(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char_p), ("dims", ctypes.c_int64 * 8), ("rank", ctypes.c_int)]
+
+
 _vp = ctypes.c_void_p
 _i64 = ctypes.c_int64
 _i64p = ctypes.POINTER(ctypes.c_int64)
@@ -154,6 +158,9 @@ SIGNATURES = {
     "onnxb200_graph_run_host_pipelined": (_int, [_vp, _vp, _int, ctypes.POINTER(_vp), ctypes.POINTER(_vp)]),
     "onnxb200_graph_output_shape": (_int, [_vp, _int, _i64p, ctypes.POINTER(_int)]),
     "onnxb200_graph_get_stats": (_int, [_vp, ctypes.POINTER(GraphStats)]),
+    "onnxb200_infer_shapes": (_int, [ctypes.POINTER(Node), _int, ctypes.POINTER(TensorInfo), _int,
+                                     ctypes.POINTER(ShapeInfo), _int, ctypes.POINTER(_int), ctypes.c_char_p,
+                                     ctypes.c_size_t]),
     "onnxb200_graph_destroy": (_int, [_vp]),
     "onnxb200_graph_profile": (_int, [_vp, _vp, ctypes.POINTER(_vp), ctypes.POINTER(_vp),
                                       ctypes.POINTER(StepProfile), _int, ctypes.POINTER(_int)]),

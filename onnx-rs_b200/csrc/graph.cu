@@ -187,70 +187,47 @@ void storage_view(const GTensor& t, std::vector<int64_t>& dims, std::vector<int6
 
 }  // namespace
 
-static void destroy_graph(onnxb200_graph* g) {
-  if (!g) return;
-  if (g->ev_inputs_read) cudaEventDestroy(g->ev_inputs_read);
-  if (g->ev_copied) cudaEventDestroy(g->ev_copied);
-  if (g->ev_begin) cudaEventDestroy(g->ev_begin);
-  if (g->ev_copy_end) cudaEventDestroy(g->ev_copy_end);
-  if (g->copy_stream) cudaStreamDestroy(g->copy_stream);
-  if (g->cge) cudaGraphExecDestroy(g->cge);
-  if (g->cg) cudaGraphDestroy(g->cg);
-  if (g->arena) cudaFree(g->arena);
-  if (g->weights) cudaFree(g->weights);
-  if (g->init) cudaFree(g->init);
-  for (void* p : g->dev_in) if (p) cudaFree(p);
-  for (void* p : g->dev_out) if (p) cudaFree(p);
-  delete g;
-}
-
-extern "C" int onnxb200_graph_destroy(onnxb200_graph* g) {
-  if (!g) return ONNXB200_ERR_INVALID_ARGUMENT;
-  // The graph may outlive its handle (and the handle's stream): wait on the
-  // whole device instead of touching the handle.
-  cudaSetDevice(g->device);
-  cudaDeviceSynchronize();
-  destroy_graph(g);
-  return ONNXB200_OK;
-}
-
-extern "C" int onnxb200_graph_build(onnxb200_handle* h, const onnxb200_node* nodes_in, int n_nodes,
-                                    const onnxb200_tensor_info* inits, int n_init,
-                                    const onnxb200_tensor_info* ins, int n_inputs,
-                                    const char* const* outs, int n_outputs, onnxb200_graph** out) {
-  if (!h || !out || (n_nodes > 0 && !nodes_in)) return ONNXB200_ERR_INVALID_ARGUMENT;
-  *out = nullptr;
-  cudaSetDevice(h->device);
-  onnxb200_graph* g = new (std::nothrow) onnxb200_graph();
-  if (!g) return ONNXB200_ERR_RESOURCE_EXHAUSTED;
-  g->h = h;
-  g->device = h->device;
-  g->n_nodes_in = n_nodes;
-  if (cudaEventCreateWithFlags(&g->ev_inputs_read, cudaEventDisableTiming) != cudaSuccess) {
-    delete g;
-    return fail(h, ONNXB200_ERR_RESOURCE_EXHAUSTED, "graph event");
-  }
+namespace {
+struct Parsed {
+  std::vector<GTensor> tensors;
   std::map<std::string, int> by_name;
+  std::vector<Node> nodes;
+  std::vector<int> order;   // topological order of node indices
+  std::vector<int> inputs;  // tensor ids of the graph inputs
+  size_t init_total = 0;    // bytes of the device copies of the initializers
+};
+}  // namespace
+
+// Parses the node list, orders it topologically and infers every tensor's
+// shape (Operator::output_shapes per node; the planner's
+// infer_node_output_shapes, src/memory/planner.rs:908-960).  Host only.
+static int parse_and_infer(const onnxb200_node* nodes_in, int n_nodes, const onnxb200_tensor_info* inits,
+                           int n_init, const onnxb200_tensor_info* ins, int n_inputs, bool need_data,
+                           Parsed& P, std::string& msg) {
+  std::map<std::string, int>& by_name = P.by_name;
   auto tensor_id = [&](const std::string& name) -> int {
     auto it = by_name.find(name);
     if (it != by_name.end()) return it->second;
     GTensor t;
     t.name = name;
-    g->tensors.push_back(t);
-    by_name[name] = (int)g->tensors.size() - 1;
-    return (int)g->tensors.size() - 1;
+    P.tensors.push_back(t);
+    by_name[name] = (int)P.tensors.size() - 1;
+    return (int)P.tensors.size() - 1;
   };
-  auto bail = [&](int code, const std::string& msg) {
-    destroy_graph(g);
-    return fail(h, code, msg);
+  auto bail = [&](int code, const std::string& m) {
+    msg = m;
+    return code;
   };
 
   // ---------------------------------------------------------------- tensors
-  size_t init_total = 0;
+  size_t& init_total = P.init_total;
   for (int i = 0; i < n_init; ++i) {
-    if (!inits[i].name || !inits[i].data) return bail(ONNXB200_ERR_INVALID_ARGUMENT, "initializer without name/data");
+    if (!inits[i].name || (need_data && !inits[i].data))
+      return bail(ONNXB200_ERR_INVALID_ARGUMENT, "initializer without name/data");
+    if (inits[i].rank < 0 || inits[i].rank > 8 || (inits[i].rank > 0 && !inits[i].shape))
+      return bail(ONNXB200_ERR_INVALID_ARGUMENT, std::string("initializer with an invalid shape: ") + inits[i].name);
     const int id = tensor_id(inits[i].name);
-    GTensor& t = g->tensors[id];
+    GTensor& t = P.tensors[id];
     t.is_init = true;
     t.init_index = i;
     t.shape.assign(inits[i].shape, inits[i].shape + inits[i].rank);
@@ -258,18 +235,26 @@ extern "C" int onnxb200_graph_build(onnxb200_handle* h, const onnxb200_node* nod
     init_total += align_up((size_t)t.numel() * 4);
   }
   for (int i = 0; i < n_inputs; ++i) {
+    if (!ins[i].name || ins[i].rank < 0 || ins[i].rank > 8 || (ins[i].rank > 0 && !ins[i].shape))
+      return bail(ONNXB200_ERR_INVALID_ARGUMENT, "graph input without name / with an invalid shape");
     const int id = tensor_id(ins[i].name);
-    GTensor& t = g->tensors[id];
+    GTensor& t = P.tensors[id];
     if (t.is_init) return bail(ONNXB200_ERR_INVALID_GRAPH, "graph input is also an initializer");
     t.is_input = true;
     t.shape.assign(ins[i].shape, ins[i].shape + ins[i].rank);
-    g->inputs.push_back(id);
+    P.inputs.push_back(id);
   }
-  std::vector<Node> nodes(n_nodes);
+  P.nodes.assign(n_nodes, Node());
+  std::vector<Node>& nodes = P.nodes;
   for (int i = 0; i < n_nodes; ++i) {
     const onnxb200_node& src = nodes_in[i];
     Node& nd = nodes[i];
     nd.op = src.op_type ? src.op_type : "";
+    if ((src.n_inputs > 0 && !src.inputs) || (src.n_outputs > 0 && !src.outputs) ||
+        (src.n_attrs > 0 && !src.attrs) || src.n_inputs < 0 || src.n_outputs < 0 || src.n_attrs < 0)
+      return bail(ONNXB200_ERR_INVALID_ARGUMENT, "node with null input / output / attribute arrays: " + nd.op);
+    for (int j = 0; j < src.n_outputs; ++j)
+      if (!src.outputs[j] || !src.outputs[j][0]) return bail(ONNXB200_ERR_INVALID_GRAPH, "node output without a name: " + nd.op);
     for (int j = 0; j < src.n_inputs; ++j) {
       const char* nm = src.inputs[j];
       nd.in.push_back((nm && nm[0]) ? tensor_id(nm) : -1);
@@ -287,20 +272,20 @@ extern "C" int onnxb200_graph_build(onnxb200_handle* h, const onnxb200_node* nod
 
   // ---------------------------------------------------------------- topological order
   // (GraphBuilder's sort, src/parser/graph_builder.rs:12-37)
-  std::vector<int> producer_node(g->tensors.size(), -1);
+  std::vector<int> producer_node(P.tensors.size(), -1);
   for (int i = 0; i < n_nodes; ++i)
     for (int t : nodes[i].out) {
-      if (producer_node[t] >= 0) return bail(ONNXB200_ERR_INVALID_GRAPH, "tensor produced twice: " + g->tensors[t].name);
+      if (producer_node[t] >= 0) return bail(ONNXB200_ERR_INVALID_GRAPH, "tensor produced twice: " + P.tensors[t].name);
       producer_node[t] = i;
     }
-  std::vector<int> order;
+  std::vector<int>& order = P.order;
   {
     std::vector<int> indeg(n_nodes, 0);
     std::vector<std::vector<int>> succ(n_nodes);
     for (int i = 0; i < n_nodes; ++i)
       for (int t : nodes[i].in) {
         if (t < 0) continue;
-        const GTensor& tt = g->tensors[t];
+        const GTensor& tt = P.tensors[t];
         if (producer_node[t] >= 0) {
           succ[producer_node[t]].push_back(i);
           indeg[i]++;
@@ -326,7 +311,7 @@ extern "C" int onnxb200_graph_build(onnxb200_handle* h, const onnxb200_node* nod
   // ---------------------------------------------------------------- shape inference
   for (int idx : order) {
     Node& nd = nodes[idx];
-    auto shp = [&](int k) -> std::vector<int64_t>& { return g->tensors[nd.in[k]].shape; };
+    auto shp = [&](int k) -> std::vector<int64_t>& { return P.tensors[nd.in[k]].shape; };
     auto need_in = [&](int k) { return (int)nd.in.size() > k && nd.in[k] >= 0; };
     std::vector<int64_t> o;
     if (nd.op == "Conv") {
@@ -415,8 +400,73 @@ extern "C" int onnxb200_graph_build(onnxb200_handle* h, const onnxb200_node* nod
       // OperatorRegistry::create_operator_for_node "not found in registry" (src/ops/registry.rs:124-127)
       return bail(ONNXB200_ERR_INVALID_OPERATOR, "operator not on this path: " + nd.op);
     }
-    g->tensors[nd.out[0]].shape = o;
+    P.tensors[nd.out[0]].shape = o;
   }
+  return ONNXB200_OK;
+}
+
+static void destroy_graph(onnxb200_graph* g) {
+  if (!g) return;
+  if (g->ev_inputs_read) cudaEventDestroy(g->ev_inputs_read);
+  if (g->ev_copied) cudaEventDestroy(g->ev_copied);
+  if (g->ev_begin) cudaEventDestroy(g->ev_begin);
+  if (g->ev_copy_end) cudaEventDestroy(g->ev_copy_end);
+  if (g->copy_stream) cudaStreamDestroy(g->copy_stream);
+  if (g->cge) cudaGraphExecDestroy(g->cge);
+  if (g->cg) cudaGraphDestroy(g->cg);
+  if (g->arena) cudaFree(g->arena);
+  if (g->weights) cudaFree(g->weights);
+  if (g->init) cudaFree(g->init);
+  for (void* p : g->dev_in) if (p) cudaFree(p);
+  for (void* p : g->dev_out) if (p) cudaFree(p);
+  delete g;
+}
+
+extern "C" int onnxb200_graph_destroy(onnxb200_graph* g) {
+  if (!g) return ONNXB200_ERR_INVALID_ARGUMENT;
+  // The graph may outlive its handle (and the handle's stream): wait on the
+  // whole device instead of touching the handle.
+  cudaSetDevice(g->device);
+  cudaDeviceSynchronize();
+  destroy_graph(g);
+  return ONNXB200_OK;
+}
+
+extern "C" int onnxb200_graph_build(onnxb200_handle* h, const onnxb200_node* nodes_in, int n_nodes,
+                                    const onnxb200_tensor_info* inits, int n_init,
+                                    const onnxb200_tensor_info* ins, int n_inputs,
+                                    const char* const* outs, int n_outputs, onnxb200_graph** out) {
+  if (!h || !out || (n_nodes > 0 && !nodes_in)) return ONNXB200_ERR_INVALID_ARGUMENT;
+  *out = nullptr;
+  cudaSetDevice(h->device);
+  onnxb200_graph* g = new (std::nothrow) onnxb200_graph();
+  if (!g) return ONNXB200_ERR_RESOURCE_EXHAUSTED;
+  g->h = h;
+  g->device = h->device;
+  g->n_nodes_in = n_nodes;
+  if (cudaEventCreateWithFlags(&g->ev_inputs_read, cudaEventDisableTiming) != cudaSuccess) {
+    delete g;
+    return fail(h, ONNXB200_ERR_RESOURCE_EXHAUSTED, "graph event");
+  }
+  Parsed P;
+  std::string pmsg;
+  {
+    const int prc = parse_and_infer(nodes_in, n_nodes, inits, n_init, ins, n_inputs, true, P, pmsg);
+    if (prc) {
+      destroy_graph(g);
+      return fail(h, prc, pmsg);
+    }
+  }
+  g->tensors = std::move(P.tensors);
+  g->inputs = P.inputs;
+  std::map<std::string, int>& by_name = P.by_name;
+  std::vector<Node>& nodes = P.nodes;
+  std::vector<int>& order = P.order;
+  size_t init_total = P.init_total;
+  auto bail = [&](int code, const std::string& msg) {
+    destroy_graph(g);
+    return fail(h, code, msg);
+  };
   for (int i = 0; i < n_outputs; ++i) {
     auto it = by_name.find(outs[i]);
     if (it == by_name.end()) return bail(ONNXB200_ERR_INVALID_GRAPH, std::string("unknown graph output: ") + outs[i]);
@@ -1382,6 +1432,43 @@ extern "C" int onnxb200_graph_output_shape(const onnxb200_graph* g, int index, i
   *rank = (int)t.shape.size();
   if (shape)
     for (size_t i = 0; i < t.shape.size(); ++i) shape[i] = t.shape[i];
+  return ONNXB200_OK;
+}
+
+extern "C" int onnxb200_infer_shapes(const onnxb200_node* nodes, int n_nodes, const onnxb200_tensor_info* known,
+                                     int n_known, onnxb200_shape_info* shapes, int max_shapes, int* n_shapes,
+                                     char* err, size_t err_len) {
+  auto report = [&](int code, const std::string& m) {
+    if (err && err_len) {
+      std::strncpy(err, m.c_str(), err_len - 1);
+      err[err_len - 1] = 0;
+    }
+    return code;
+  };
+  if (err && err_len) err[0] = 0;
+  if (!n_shapes || n_nodes < 0 || n_known < 0 || (n_nodes > 0 && !nodes) || (n_known > 0 && !known) ||
+      (max_shapes > 0 && !shapes))
+    return report(ONNXB200_ERR_INVALID_ARGUMENT, "onnxb200_infer_shapes: null or negative argument");
+  *n_shapes = 0;
+  // Every known tensor is treated as an initializer: only its shape is read.
+  Parsed P;
+  std::string msg;
+  int rc = parse_and_infer(nodes, n_nodes, known, n_known, nullptr, 0, false, P, msg);
+  if (rc) return report(rc, msg);
+  int n = 0;
+  for (int i = 0; i < n_nodes; ++i)
+    for (size_t j = 0; j < P.nodes[i].out.size(); ++j, ++n) {
+      if (n >= max_shapes) continue;
+      const GTensor& t = P.tensors[P.nodes[i].out[j]];
+      onnxb200_shape_info& o = shapes[n];
+      o.name = nodes[i].outputs[j];
+      o.rank = (int)t.shape.size();
+      for (int d = 0; d < 8; ++d) o.dims[d] = d < o.rank ? t.shape[d] : 0;
+    }
+  *n_shapes = n;
+  if (n > max_shapes)
+    return report(ONNXB200_ERR_RESOURCE_EXHAUSTED, "onnxb200_infer_shapes: " + std::to_string(n) +
+                                                       " node outputs, room for " + std::to_string(max_shapes));
   return ONNXB200_OK;
 }
 

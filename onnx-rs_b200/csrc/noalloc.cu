@@ -31,28 +31,59 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
 
 constexpr int kMaxDevices = 64;
 std::mutex g_setup_mutex;
-unsigned char* g_scratch_ptr[kMaxDevices] = {};  // device address, per device
-int g_num_sms[kMaxDevices] = {};
+struct DeviceState {
+  unsigned char* scratch = nullptr;  // device address of g_noalloc_scratch
+  int num_sms = 0;
+  // Recorded on the caller's stream after each call's kernels: the next call
+  // waits for it (bounded) before it rewrites the array, so a call that gave up
+  // waiting (ONNXB200_ERR_TIMEOUT) never has its packed weights overwritten
+  // while its kernels still read them.
+  cudaEvent_t done = nullptr;
+  // A non-blocking stream of the library's own for reading the status word, so
+  // that the read waits neither for the caller's later work nor for other
+  // threads' work on the legacy default stream.
+  cudaStream_t status_stream = nullptr;
+};
+DeviceState g_dev[kMaxDevices];
 
 // Host code cannot use g_noalloc_scratch as a pointer (it names the host-side
 // shadow of the symbol), so the device address is looked up once per device,
-// with that device current.
-int setup_device(int dev, unsigned char** ptr, int* num_sms) {
+// with that device current.  The event and stream are created then too (neither
+// allocates device memory).
+int setup_device(int dev, DeviceState** out) {
   if (dev < 0 || dev >= kMaxDevices) return ONNXB200_ERR_UNSUPPORTED;
   std::lock_guard<std::mutex> lock(g_setup_mutex);
-  if (!g_scratch_ptr[dev]) {
+  DeviceState& st = g_dev[dev];
+  if (!st.scratch) {
     void* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess || !p) return ONNXB200_ERR_EXECUTION;
     int sms = 0;
     e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return ONNXB200_ERR_EXECUTION;
-    g_scratch_ptr[dev] = static_cast<unsigned char*>(p);
-    g_num_sms[dev] = sms;
+    if (!st.done && cudaEventCreateWithFlags(&st.done, cudaEventDisableTiming) != cudaSuccess)
+      return ONNXB200_ERR_EXECUTION;
+    if (!st.status_stream &&
+        cudaStreamCreateWithFlags(&st.status_stream, cudaStreamNonBlocking) != cudaSuccess)
+      return ONNXB200_ERR_EXECUTION;
+    st.num_sms = sms;
+    st.scratch = static_cast<unsigned char*>(p);
   }
-  *ptr = g_scratch_ptr[dev];
-  *num_sms = g_num_sms[dev];
+  *out = &st;
   return ONNXB200_OK;
+}
+
+// Polls `ev` until it has completed or `timeout_ms` passed.
+int wait_event_bounded(cudaEvent_t ev, int timeout_ms) {
+  const auto t0 = std::chrono::steady_clock::now();
+  while (true) {
+    cudaError_t q = cudaEventQuery(ev);
+    if (q == cudaSuccess) return ONNXB200_OK;
+    if (q != cudaErrorNotReady) return ONNXB200_ERR_EXECUTION;
+    if (std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(timeout_ms))
+      return ONNXB200_ERR_TIMEOUT;
+    std::this_thread::sleep_for(std::chrono::microseconds(20));
+  }
 }
 
 }  // namespace
@@ -66,21 +97,27 @@ extern "C" int onnxb200_conv2d_nhwc_noalloc(void* cuda_stream, const onnxb200_co
   if (d->layout != ONNXB200_LAYOUT_NHWC) return ONNXB200_ERR_VALIDATION;  // NCHW would need repack scratch
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return ONNXB200_ERR_EXECUTION;
-  unsigned char* scratch = nullptr;
-  int num_sms = 0;
-  int rc = setup_device(dev, &scratch, &num_sms);
+  // The call blocks until y is written, which a capturing stream cannot do.
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(static_cast<cudaStream_t>(cuda_stream), &cap) != cudaSuccess)
+    return ONNXB200_ERR_EXECUTION;
+  if (cap != cudaStreamCaptureStatusNone) return ONNXB200_ERR_UNSUPPORTED;
+  DeviceState* ds = nullptr;
+  int rc = setup_device(dev, &ds);
   if (rc) return rc;
+  unsigned char* scratch = ds->scratch;
+  constexpr int kTimeoutMs = 60000;
 
   // A handle-shaped view over the caller's stream and the fixed scratch; no
   // device memory is allocated for it.
   onnxb200_handle view;
   view.device = dev;
-  view.num_sms = num_sms;
+  view.num_sms = ds->num_sms;
   view.stream = static_cast<cudaStream_t>(cuda_stream);
   view.own_stream = nullptr;
   view.d_status = reinterpret_cast<int*>(scratch);
   view.opts.precision = ONNXB200_PREC_3XTF32;
-  view.opts.wait_timeout_ms = 60000;
+  view.opts.wait_timeout_ms = kTimeoutMs;
 
   onnxb200_conv_desc r;
   int64_t oh = 0, ow = 0;
@@ -97,6 +134,11 @@ extern "C" int onnxb200_conv2d_nhwc_noalloc(void* cuda_stream, const onnxb200_co
   if (rc) return rc;
   if (need > kScratchBytes - kStatusBytes) return ONNXB200_ERR_RESOURCE_EXHAUSTED;
 
+  // The previous call on this device (possibly one that timed out) must be
+  // done with the array before it is rewritten.
+  rc = wait_event_bounded(ds->done, kTimeoutMs);
+  if (rc) return rc;
+
   // The status word must start at zero; the packed weights and epilogue
   // vectors are fully rewritten below, so the rest needs no clearing.
   if (cudaMemsetAsync(view.d_status, 0, sizeof(int), view.stream) != cudaSuccess)
@@ -104,23 +146,20 @@ extern "C" int onnxb200_conv2d_nhwc_noalloc(void* cuda_stream, const onnxb200_co
   size_t used = 0;
   rc = ob2::conv_plan_init(&view, d, (int)r.c, w, bias, bn_scale, bn_bias, bn_mean, bn_var, &plan,
                            scratch + kStatusBytes, kScratchBytes - kStatusBytes, &used);
-  if (rc) return rc;
-  rc = ob2::conv_plan_exec_nhwc(&view, &plan, x, residual, y);
+  if (rc == ONNXB200_OK) rc = ob2::conv_plan_exec_nhwc(&view, &plan, x, residual, y);
+  // recorded even after a failed launch, so the next call's wait ends
+  if (cudaEventRecord(ds->done, view.stream) != cudaSuccess) return ONNXB200_ERR_EXECUTION;
   if (rc) return rc;
 
   // Blocking: return once y is written, so that sequential calls never share
-  // the array while one of them is still running.  The wait is bounded.
-  const auto t0 = std::chrono::steady_clock::now();
-  while (true) {
-    cudaError_t q = cudaStreamQuery(view.stream);
-    if (q == cudaSuccess) break;
-    if (q != cudaErrorNotReady) return ONNXB200_ERR_EXECUTION;
-    if (std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(view.opts.wait_timeout_ms))
-      return ONNXB200_ERR_TIMEOUT;
-    std::this_thread::sleep_for(std::chrono::microseconds(20));
-  }
+  // the array while one of them is still running.  The wait is bounded; after
+  // a timeout the next call first waits for this one's kernels.
+  rc = wait_event_bounded(ds->done, kTimeoutMs);
+  if (rc) return rc;
   int status = 0;
-  if (cudaMemcpy(&status, view.d_status, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+  if (cudaMemcpyAsync(&status, view.d_status, sizeof(int), cudaMemcpyDeviceToHost, ds->status_stream) !=
+          cudaSuccess ||
+      cudaStreamSynchronize(ds->status_stream) != cudaSuccess)
     return ONNXB200_ERR_EXECUTION;
   return status;
 }

@@ -58,6 +58,38 @@ def _c_node(nd: dict, keep: list) -> C.Node:
     return n
 
 
+def _c_shapes(shapes: Dict[str, Sequence[int]], keep: list):
+    arr = (C.TensorInfo * max(1, len(shapes)))()
+    for i, (name, shp) in enumerate(shapes.items()):
+        t = arr[i]
+        t.name = name.encode()
+        keep.append(t.name)
+        dims = C.i64_array(shp)
+        keep.append(dims)
+        t.shape = ctypes.cast(dims, ctypes.POINTER(ctypes.c_int64))
+        t.rank = len(shp)
+    return arr
+
+
+def infer_shapes(nodes: Sequence[dict], known: Dict[str, Sequence[int]]) -> Dict[str, List[int]]:
+    """Shapes of every node output of a node list, without building a graph
+    (``onnxb200_infer_shapes``; the planner's infer_node_output_shapes,
+    src/memory/planner.rs:908-960).  ``known`` maps initializer and graph-input
+    names to their shapes.  Host only: no handle, no GPU."""
+    from .runtime import raise_for
+    keep: list = []
+    cnodes = (C.Node * max(1, len(nodes)))(*[_c_node(nd, keep) for nd in nodes])
+    ck = _c_shapes(dict(known), keep)
+    n_out = sum(len(nd["outputs"]) for nd in nodes)
+    out = (C.ShapeInfo * max(1, n_out))()
+    n = ctypes.c_int()
+    err = ctypes.create_string_buffer(512)
+    rc = C.lib().onnxb200_infer_shapes(cnodes, len(nodes), ck, len(known), out, n_out, ctypes.byref(n), err, 512)
+    if rc:
+        raise_for(rc, err.value.decode(errors="replace"))
+    return {out[i].name.decode(): [int(out[i].dims[d]) for d in range(out[i].rank)] for i in range(n.value)}
+
+
 class Graph:
     def __init__(self, handle: Handle, nodes: Sequence[dict], initializers: Dict[str, np.ndarray],
                  inputs: Sequence[Tuple[str, Sequence[int]]], outputs: Sequence[str]):

@@ -185,3 +185,37 @@ def test_workload_graphs_are_well_formed(ob):
     assert abs(ob.workloads.resnet50.conv_flops_per_image / 2 - 4.09e9) / 4.09e9 < 0.02
     nodes, _, _, _ = ob.workloads.resnet18(batch=1)
     assert sum(1 for n in nodes if n["op"] == "Conv") == 20
+
+
+def test_infer_shapes_matches_oracle(ob, oracle):
+    """onnxb200_infer_shapes gives every node output's shape of ResNet-18 (node
+    list, no graph, no GPU) equal to the shape the oracle computes."""
+    nodes, inits, ins, outs = ob.workloads.resnet18(batch=1, seed=2)
+    known = {k: list(v.shape) for k, v in inits.items()}
+    known.update({n: s for n, s in ins})
+    shapes = ob.infer_shapes(nodes, known)
+    names = [o for nd in nodes for o in nd["outputs"]]
+    assert list(shapes) == names
+    ref = oracle.run_graph(nodes, inits, {"X": ob.workloads.resnet_input(2, 1)}, names)
+    for n in names:
+        assert shapes[n] == list(ref[n].shape), n
+    assert shapes["logits"] == [1, 1000]
+    # a batch of 256 without building anything
+    known["X"] = [256, 3, 224, 224]
+    assert ob.infer_shapes(nodes, known)["logits"] == [256, 1000]
+
+
+def test_infer_shapes_errors(ob):
+    C = ob._capi
+    conv = {"op": "Conv", "inputs": ["X", "W"], "outputs": ["Y"], "attrs": {"pads": [1, 1, 1, 1]}}
+    with pytest.raises(ob.ValidationError):  # channel mismatch
+        ob.infer_shapes([conv], {"X": [1, 8, 5, 5], "W": [4, 3, 3, 3]})
+    with pytest.raises(ob.InvalidOperator):
+        ob.infer_shapes([{"op": "Softmax", "inputs": ["X"], "outputs": ["Y"]}], {"X": [2, 3]})
+    with pytest.raises(ob.InvalidGraph):  # input without a producer or a shape
+        ob.infer_shapes([conv], {"W": [4, 8, 3, 3]})
+    assert ob.infer_shapes([conv], {"X": [2, 8, 5, 5], "W": [4, 8, 3, 3]}) == {"Y": [2, 4, 5, 5]}
+    n = ctypes.c_int()
+    assert C.lib().onnxb200_infer_shapes(None, 0, None, 0, None, 0, None, None, 0) == C.ERR_INVALID_ARGUMENT
+    assert C.lib().onnxb200_infer_shapes(None, 0, None, 0, None, 0, ctypes.byref(n), None, 0) == C.OK
+    assert n.value == 0

@@ -27,6 +27,10 @@ def test_reference_arm_json_line():
     assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["cores"] >= 1
     assert d["cpu_baseline"]["value"] == d["value"]
     assert d["e2e"] == {"value": d["value"], "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+    # the line describes what ran: the sample batch and the measured time of one pass over it
+    n = d["config"]["global_batch"]
+    assert n == d["config"]["per_step_batch"] == d["cpu_baseline"]["cores"]
+    assert abs(d["ms_per_step"] - 1000.0 * n / d["value"]) <= 1e-6 * d["ms_per_step"]
 
 
 def test_reference_arm_silent_on_other_ranks():

@@ -1,10 +1,22 @@
 """GPU end-to-end tests of the graph executor against the oracle evaluating the
 same unfused node list node by node.
 
-End-to-end logits: an element passes if |a-b| <= 1e-3 * max|ref| or
-|a-b|/|b| <= 1e-3 (3xTF32); 2e-2 for the tf32 / bf16 fast modes.  The absolute
-term is scaled by the logits' magnitude because the randomly initialised
-networks (BatchNormalization gamma = 1 everywhere) grow activations to ~1e4.
+End-to-end logits, 3xTF32 (and the fp32 CUDA-core mode).  The ground truth is
+the oracle with fp64 accumulation (``acc64``); the reference-faithful oracle
+(fp32, the reference's summation order) gives the error of the reference's own
+arithmetic on the same images.  A logit passes if it meets the reference's rule
+(src/tools/comparison.rs:1298-1321) at 1e-3 -- |a-b| <= 1e-3 or |a-b|/|b| <= 1e-3,
+no scaling -- or if its error is within the largest error of the reference's
+own fp32 arithmetic on the same checked logits.  The second clause exists
+because the randomly initialised networks (BatchNormalization gamma = 1, as the
+workload specifies) grow activations to ~1e4: a logit of size ~1 then carries an
+fp32 rounding error near 1e-2 whoever computes it, and the fp32 oracle itself
+fails the plain 1e-3 rule on such logits (its failures are counted and printed
+beside the GPU's).
+
+Fast modes (tf32, bf16): their operands carry 10 or 7 mantissa bits, so the
+logits' error is a fraction of the logits' scale, not of each logit: per image,
+max|a - b| <= 2e-2 * max|b| against the fp64 oracle.
 """
 import importlib
 
@@ -18,12 +30,49 @@ pytestmark = pytest.mark.gpu
 
 ob_mod = importlib.import_module("onnx-rs_b200")
 
+TOL_E2E = 1e-3
+TOL_FAST = 2e-2
 
-def check_logits(y, ref, tol, what):
-    scale = float(np.abs(ref).max())
-    n, ma, mr = compare(y, ref, tol, tol * scale)
-    assert n == 0, f"{what}: {n} logits outside tolerance (max abs {ma:.3g} vs scale {scale:.3g}, max rel {mr:.3g})"
-    return ma / scale
+
+def check_logits_3x(y, r32, r64, what):
+    """Element-wise check of fp32-accuracy logits against the fp64 oracle (r64),
+    with the fp32 oracle's (r32) own error as the documented bound for logits
+    that the plain 1e-3 rule cannot hold (see the module docstring)."""
+    y = np.asarray(y, np.float64)
+    r64 = np.asarray(r64, np.float64)
+    e_ref = np.abs(np.asarray(r32, np.float64) - r64)
+    bound = float(e_ref.max())
+    n_gpu, ma_gpu, mr_gpu = compare(y, r64, TOL_E2E, TOL_E2E)
+    n_ref, ma_ref, mr_ref = compare(r32, r64, TOL_E2E, TOL_E2E)
+    d = np.abs(y - r64)
+    rel = d / np.maximum(np.abs(r64), 1e-30)
+    ok = (d <= TOL_E2E) | ((rel <= TOL_E2E) & (np.abs(r64) > 1e-6)) | (d <= bound)
+    n_bad = int((~ok).sum())
+    msg = (f"{what}: {y.size} logits; plain 1e-3 rule: GPU {n_gpu} fail (max abs {ma_gpu:.3g}, max rel "
+           f"{mr_gpu:.3g}), fp32 oracle {n_ref} fail (max abs {ma_ref:.3g}, max rel {mr_ref:.3g}); "
+           f"bound = fp32 oracle's max error {bound:.3g}; {n_bad} GPU logits beyond both")
+    print(msg)
+    assert n_bad == 0, msg
+    return n_gpu, n_ref, ma_gpu, ma_ref
+
+
+def check_logits_fast(y, r64, what):
+    y = np.asarray(y, np.float64).reshape(len(r64), -1)
+    r64 = np.asarray(r64, np.float64).reshape(len(r64), -1)
+    worst = 0.0
+    for i in range(len(r64)):
+        scale = float(np.abs(r64[i]).max())
+        worst = max(worst, float(np.abs(y[i] - r64[i]).max()) / scale)
+    n_el, _, _ = compare(y, r64, TOL_FAST, TOL_FAST)
+    msg = (f"{what}: max over images of max|a-b|/max|b| = {worst:.3g} (bar {TOL_FAST}); "
+           f"{n_el} of {y.size} logits outside the element-wise 2e-2 rule")
+    print(msg)
+    assert worst <= TOL_FAST, msg
+
+
+def oracle_logits(oracle, nodes1, inits1, x, outs, images, acc64):
+    """Oracle logits of the given images (the oracle threads over the batch)."""
+    return oracle.run_graph(nodes1, inits1, {"X": np.ascontiguousarray(x[images])}, outs, acc64=acc64)[outs[0]]
 
 
 @pytest.fixture(scope="module")
@@ -31,12 +80,13 @@ def r18_ref(oracle):
     nodes, inits, ins, outs = ob_mod.workloads.resnet18(batch=2, seed=2)
     x = ob_mod.workloads.resnet_input(2, 2)
     ref = oracle.run_graph(nodes, inits, {"X": x}, outs)[outs[0]]
-    return nodes, inits, ins, outs, x, ref
+    ref64 = oracle.run_graph(nodes, inits, {"X": x}, outs, acc64=True)[outs[0]]
+    return nodes, inits, ins, outs, x, ref, ref64
 
 
-@pytest.mark.parametrize("precision,tol", [("3xtf32", 1e-3), ("fp32", 1e-3), ("tf32", 2e-2), ("bf16", 2e-2)])
-def test_resnet18_graph(ob, r18_ref, precision, tol):
-    nodes, inits, ins, outs, x, ref = r18_ref
+@pytest.mark.parametrize("precision", ["3xtf32", "fp32", "tf32", "bf16"])
+def test_resnet18_graph(ob, r18_ref, precision):
+    nodes, inits, ins, outs, x, ref, ref64 = r18_ref
     h = ob.Handle(0, precision=precision)
     g = ob.Graph(h, nodes, inits, ins, outs)
     st = g.stats()
@@ -48,7 +98,10 @@ def test_resnet18_graph(ob, r18_ref, precision, tol):
     h.synchronize()
     np.testing.assert_array_equal(y_eager.cpu().numpy(), y_graph.cpu().numpy())
     np.testing.assert_array_equal(y_graph.cpu().numpy(), y_replay.cpu().numpy())
-    check_logits(y_replay.cpu().numpy(), ref, tol, f"resnet18/{precision}")
+    if precision in ("3xtf32", "fp32"):
+        check_logits_3x(y_replay.cpu().numpy(), ref, ref64, f"resnet18/{precision}")
+    else:
+        check_logits_fast(y_replay.cpu().numpy(), ref64, f"resnet18/{precision}")
     # host buffers in / out
     yh = g.run_host([x])[0]
     np.testing.assert_array_equal(yh, y_replay.cpu().numpy())
@@ -71,7 +124,7 @@ def test_graph_from_onnx_model(ob, r18_ref, tmp_path):
     """A .onnx file (weights in an external data file, symbolic batch
     dimension) read by onnxb200_model_load and built by
     onnxb200_graph_build_from_model runs exactly like the node-list graph."""
-    nodes, inits, ins, outs, x, ref = r18_ref
+    nodes, inits, ins, outs, x, ref, ref64 = r18_ref
     h = ob.Handle(0, precision="3xtf32")
     g_nodes = ob.Graph(h, nodes, inits, ins, outs)
     xin = torch.from_numpy(x).cuda()
@@ -87,14 +140,14 @@ def test_graph_from_onnx_model(ob, r18_ref, tmp_path):
     assert g.stats()["n_fused"] == g_nodes.stats()["n_fused"]
     y = g.run([xin])[0].cpu().numpy()
     np.testing.assert_array_equal(y, y_nodes)
-    check_logits(y, ref, 1e-3, "resnet18 from .onnx")
+    check_logits_3x(y, ref, ref64, "resnet18 from .onnx")
     g.close()
     g_nodes.close()
     h.close()
 
 
-def test_resnet18_full_batch_config(ob, oracle, r18_ref):
-    """ResNet-18 at batch 32 (seed 2): images 0 and 31 against the oracle."""
+def test_resnet18_full_batch_config(ob, oracle):
+    """ResNet-18 at batch 32 (seed 2), 3xTF32: every image against the oracle."""
     nodes, inits, ins, outs = ob.workloads.resnet18(batch=32, seed=2)
     x = ob.workloads.resnet_input(2, 32)
     h = ob.Handle(0, precision="3xtf32")
@@ -102,18 +155,33 @@ def test_resnet18_full_batch_config(ob, oracle, r18_ref):
     y = g.run([torch.from_numpy(x).cuda()])[0]
     h.synchronize()
     y = y.cpu().numpy()
-    n1, i1, _, _ = ob.workloads.resnet18(batch=1, seed=2)
-    for i in (0, 31):
-        ref = oracle.run_graph(n1, i1, {"X": x[i:i + 1]}, outs)[outs[0]]
-        check_logits(y[i:i + 1], ref, 1e-3, f"resnet18 b32 image {i}")
     g.close()
     h.close()
+    n32, i32, _, _ = ob.workloads.resnet18(batch=32, seed=2)
+    imgs = np.arange(32)
+    r32 = oracle_logits(oracle, n32, i32, x, outs, imgs, False)
+    r64 = oracle_logits(oracle, n32, i32, x, outs, imgs, True)
+    check_logits_3x(y, r32, r64, "resnet18 b32, all 32 images")
 
 
-def test_resnet50_full_batch_config(ob, oracle):
-    """ResNet-50 v1.5 at batch 256 (seed 4), 3xTF32: images 0 and 255 against the oracle."""
-    nodes, inits, ins, outs = ob.workloads.resnet50(batch=256, seed=4)
-    x = ob.workloads.resnet_input(4, 256)
+@pytest.fixture(scope="module")
+def r50_b256():
+    nodes, inits, ins, outs = ob_mod.workloads.resnet50(batch=256, seed=4)
+    x = ob_mod.workloads.resnet_input(4, 256)
+    return nodes, inits, ins, outs, x
+
+
+@pytest.fixture(scope="module")
+def r50_b256_ref64(oracle, r50_b256):
+    """fp64-accumulation oracle logits of all 256 images."""
+    nodes, inits, ins, outs, x = r50_b256
+    return oracle_logits(oracle, nodes, inits, x, outs, np.arange(256), True)
+
+
+def test_resnet50_full_batch_config(ob, oracle, r50_b256, r50_b256_ref64):
+    """ResNet-50 v1.5 at batch 256 (seed 4), 3xTF32: all 256 images against the
+    oracle (M-tiles span image boundaries, so every tile of every layer is covered)."""
+    nodes, inits, ins, outs, x = r50_b256
     h = ob.Handle(0, precision="3xtf32")
     g = ob.Graph(h, nodes, inits, ins, outs)
     st = g.stats()
@@ -121,23 +189,21 @@ def test_resnet50_full_batch_config(ob, oracle):
     y = g.run([torch.from_numpy(x).cuda()])[0]
     h.synchronize()
     y = y.cpu().numpy()
-    n1, i1, _, _ = ob.workloads.resnet50(batch=1, seed=4)
-    for i in (0, 255):
-        ref = oracle.run_graph(n1, i1, {"X": x[i:i + 1]}, outs)[outs[0]]
-        check_logits(y[i:i + 1], ref, 1e-3, f"resnet50 b256 image {i}")
     g.close()
     h.close()
+    r32 = oracle_logits(oracle, nodes, inits, x, outs, np.arange(256), False)
+    check_logits_3x(y, r32, r50_b256_ref64, "resnet50 b256, all 256 images")
 
 
 @pytest.mark.parametrize("precision", ["tf32", "bf16"])
-def test_resnet50_fast_modes(ob, oracle, precision):
-    nodes, inits, ins, outs = ob.workloads.resnet50(batch=2, seed=4)
-    x = ob.workloads.resnet_input(4, 2)
-    ref = oracle.run_graph(nodes, inits, {"X": x}, outs)[outs[0]]
+def test_resnet50_fast_modes(ob, oracle, r50_b256, r50_b256_ref64, precision):
+    """The fast modes on the batch-256 configuration, every image against the
+    fp64 oracle at the fast-mode bar."""
+    nodes, inits, ins, outs, x = r50_b256
     h = ob.Handle(0, precision=precision)
     g = ob.Graph(h, nodes, inits, ins, outs)
     y = g.run([torch.from_numpy(x).cuda()])[0]
     h.synchronize()
-    check_logits(y.cpu().numpy(), ref, 2e-2, f"resnet50/{precision}")
+    check_logits_fast(y.cpu().numpy(), r50_b256_ref64, f"resnet50 b256/{precision}")
     g.close()
     h.close()

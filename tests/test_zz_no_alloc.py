@@ -109,3 +109,21 @@ def test_noalloc_rejects_what_it_cannot_hold():
     d2.layout = C.LAYOUT_NCHW
     rc, _ = run_noalloc(d2, x, w, b, bn, res, shape)
     assert rc == C.ERR_VALIDATION
+
+
+def test_noalloc_refuses_a_capturing_stream():
+    """The entry point blocks until y is written, which a stream under capture
+    cannot do: it returns ERR_UNSUPPORTED there and leaves the capture intact."""
+    d, x, w, b, bn, res, shape = make_case(5, 1, 16, 8, 16, 3, 1, with_bn=False, with_res=False)
+    y = torch.zeros(shape, dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        rc = C.lib().onnxb200_conv2d_nhwc_noalloc(s, ctypes.byref(d), p(x), p(w), p(b), None, None, None, None,
+                                                   None, p(y))
+        y.add_(1.0)
+    assert rc == C.ERR_UNSUPPORTED
+    graph.replay()
+    torch.cuda.synchronize()
+    assert float(y.min()) == 1.0 and float(y.max()) == 1.0
