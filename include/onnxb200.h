@@ -382,6 +382,46 @@ ONNXB200_API int onnxb200_graph_profile(onnxb200_handle* h, onnxb200_graph* g,
 ONNXB200_API int onnxb200_graph_get_stats(const onnxb200_graph* g, onnxb200_graph_stats* st);
 ONNXB200_API int onnxb200_graph_destroy(onnxb200_graph* g);
 
+/* ---------------------------------------------------------------- several GPUs */
+/* Batch-sharded replicas of one graph on several GPUs of this process, for a
+ * host that drives all of them from one process (one process per GPU can
+ * instead build one graph per process on its own slice).  Every graph input is
+ * split along its first dimension into contiguous slices, one per device (the
+ * first batch % n_devices devices take one image more); each device holds a full
+ * copy of the packed weights; there is no collective.  The reference runs one
+ * graph on host cores (ExecutionEngine::run_concurrent,
+ * src/execution/engine.rs:743-809) and has no multi-device path.
+ * inputs[] carry the FULL batch shapes; every output must have the batch as its
+ * first dimension.  opts as for onnxb200_create (NULL = defaults).  Builds the
+ * devices in parallel, one host thread each. */
+typedef struct onnxb200_multi onnxb200_multi;
+ONNXB200_API int onnxb200_multi_build(const int* devices, int n_devices, const onnxb200_options* opts,
+                                      const onnxb200_node* nodes, int n_nodes,
+                                      const onnxb200_tensor_info* initializers, int n_init,
+                                      const onnxb200_tensor_info* inputs, int n_inputs,
+                                      const char* const* outputs, int n_outputs, onnxb200_multi** out,
+                                      char* err, size_t err_len);
+/* Runs n_batches full batches from HOST buffers (inputs[b * n_inputs + i],
+ * outputs[b * n_outputs + o]; pinned memory lets the copies overlap): one host
+ * thread per device copies its rows of each input in, replays its graph
+ * (onnxb200_graph_run_host_pipelined) and copies its rows of each output into
+ * the disjoint rows of the caller's output buffers.  The threads start together
+ * from a host barrier; each device's time from that release to its last
+ * completion event is kept for onnxb200_multi_get_info.  Returns when every
+ * device is done (bounded waits as onnxb200_synchronize). */
+ONNXB200_API int onnxb200_multi_run_host(onnxb200_multi* m, int n_batches, const float* const* inputs,
+                                         float* const* outputs);
+/* n_devices, batch, slice_begin[n_devices] (first image of each device's slice)
+ * and last_run_ms[n_devices] (the last run's device time per device); any
+ * pointer may be NULL. */
+ONNXB200_API int onnxb200_multi_get_info(const onnxb200_multi* m, int* n_devices, int64_t* batch,
+                                         int64_t* slice_begin, float* last_run_ms);
+/* Full-batch shape of output `index`. */
+ONNXB200_API int onnxb200_multi_output_shape(const onnxb200_multi* m, int index, int64_t* shape, int* rank);
+/* Message of the last failed run ("" if none). */
+ONNXB200_API const char* onnxb200_multi_last_error(const onnxb200_multi* m);
+ONNXB200_API int onnxb200_multi_destroy(onnxb200_multi* m);
+
 /* ---------------------------------------------------------------- ONNX models */
 /* A parsed .onnx ModelProto, host memory only (no handle, no GPU needed):
  * OnnxModelLoader (src/parser/model_loader.rs:27-454) restricted to the main

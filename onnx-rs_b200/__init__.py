@@ -12,7 +12,7 @@ from .runtime import (Handle, OnnxB200Error, ValidationError, ExecutionError, Un
                       InvalidModel)
 from .ops import (ExecutionContext, Operator, OperatorRegistry, Conv, ConvPlan, MatMul, Gemm, MaxPool,
                   GlobalAveragePool, Relu, Add, BatchNormalization, Flatten)
-from .graph import Graph, infer_shapes
+from .graph import Graph, MultiGraph, infer_shapes
 from . import onnx_io, sharding, synth, workloads
 
 LIB_PATH = _capi.LIB_PATH
@@ -20,5 +20,5 @@ LIB_PATH = _capi.LIB_PATH
 __all__ = ["Handle", "OnnxB200Error", "ValidationError", "ExecutionError", "UnsupportedFeature",
            "OperationTimeout", "ResourceExhausted", "InvalidGraph", "InvalidOperator", "ExecutionContext",
            "Operator", "OperatorRegistry", "Conv", "ConvPlan", "MatMul", "Gemm", "MaxPool", "GlobalAveragePool", "Relu",
-           "Add", "BatchNormalization", "Flatten", "Graph", "infer_shapes", "onnx_io", "synth", "workloads", "LIB_PATH",
+           "Add", "BatchNormalization", "Flatten", "Graph", "MultiGraph", "infer_shapes", "onnx_io", "synth", "workloads", "LIB_PATH",
            "IoError", "ProtobufError", "InvalidModel"]

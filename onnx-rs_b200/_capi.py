@@ -158,6 +158,15 @@ SIGNATURES = {
     "onnxb200_graph_run_host_pipelined": (_int, [_vp, _vp, _int, ctypes.POINTER(_vp), ctypes.POINTER(_vp)]),
     "onnxb200_graph_output_shape": (_int, [_vp, _int, _i64p, ctypes.POINTER(_int)]),
     "onnxb200_graph_get_stats": (_int, [_vp, ctypes.POINTER(GraphStats)]),
+    "onnxb200_multi_build": (_int, [ctypes.POINTER(_int), _int, ctypes.POINTER(Options), ctypes.POINTER(Node), _int,
+                                    ctypes.POINTER(TensorInfo), _int, ctypes.POINTER(TensorInfo), _int,
+                                    ctypes.POINTER(ctypes.c_char_p), _int, ctypes.POINTER(_vp), ctypes.c_char_p,
+                                    ctypes.c_size_t]),
+    "onnxb200_multi_run_host": (_int, [_vp, _int, ctypes.POINTER(_vp), ctypes.POINTER(_vp)]),
+    "onnxb200_multi_get_info": (_int, [_vp, ctypes.POINTER(_int), _i64p, _i64p, ctypes.POINTER(_f32)]),
+    "onnxb200_multi_output_shape": (_int, [_vp, _int, _i64p, ctypes.POINTER(_int)]),
+    "onnxb200_multi_last_error": (ctypes.c_char_p, [_vp]),
+    "onnxb200_multi_destroy": (_int, [_vp]),
     "onnxb200_infer_shapes": (_int, [ctypes.POINTER(Node), _int, ctypes.POINTER(TensorInfo), _int,
                                      ctypes.POINTER(ShapeInfo), _int, ctypes.POINTER(_int), ctypes.c_char_p,
                                      ctypes.c_size_t]),

@@ -246,3 +246,100 @@ class Graph:
             self.close()
         except Exception:
             pass
+
+
+class MultiGraph:
+    """Batch-sharded replicas of one graph on several GPUs of this process
+    (``onnxb200_multi_build``): every input is split along its first dimension
+    into contiguous slices, one per device, each device holds a full copy of
+    the packed weights, and there is no collective.  ``run_host`` drives one
+    host thread per device; each copies its rows in, replays its graph and
+    copies its rows of the outputs into disjoint rows of the host outputs."""
+
+    def __init__(self, devices: Sequence[int], nodes: Sequence[dict], initializers: Dict[str, np.ndarray],
+                 inputs: Sequence[Tuple[str, Sequence[int]]], outputs: Sequence[str],
+                 precision: str | int = "3xtf32", use_cuda_graph: bool = True):
+        from .runtime import raise_for
+        self.lib = C.lib()
+        opts = C.Options()
+        self.lib.onnxb200_default_options(ctypes.byref(opts))
+        opts.precision = C.PRECISIONS[precision] if isinstance(precision, str) else int(precision)
+        opts.use_cuda_graph = 1 if use_cuda_graph else 0
+        keep: list = []
+        cnodes = (C.Node * max(1, len(nodes)))(*[_c_node(nd, keep) for nd in nodes])
+        arrs = {k: np.ascontiguousarray(v, dtype=np.float32) for k, v in initializers.items()}
+        inits = (C.TensorInfo * max(1, len(arrs)))()
+        for i, (name, a) in enumerate(arrs.items()):
+            t = inits[i]
+            t.name = name.encode()
+            shp = C.i64_array(a.shape)
+            keep += [t.name, shp]
+            t.data = a.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+            t.shape = ctypes.cast(shp, ctypes.POINTER(ctypes.c_int64))
+            t.rank = a.ndim
+        ins = _c_shapes({n: list(s) for n, s in inputs}, keep)
+        onames = [o.encode() for o in outputs]
+        out_arr = (ctypes.c_char_p * max(1, len(onames)))(*onames)
+        devs = (ctypes.c_int * len(devices))(*devices)
+        err = ctypes.create_string_buffer(512)
+        ptr = ctypes.c_void_p()
+        rc = self.lib.onnxb200_multi_build(devs, len(devices), ctypes.byref(opts), cnodes, len(nodes), inits,
+                                           len(arrs), ins, len(inputs), out_arr, len(onames), ctypes.byref(ptr),
+                                           err, 512)
+        if rc:
+            raise_for(rc, err.value.decode(errors="replace"))
+        self.ptr = ptr
+        self.devices = list(devices)
+        self.input_specs = [(n, list(s)) for n, s in inputs]
+        self.output_shapes = []
+        for i in range(len(onames)):
+            shp = C.i64_array([0] * 8)
+            r = ctypes.c_int()
+            self.lib.onnxb200_multi_output_shape(self.ptr, i, shp, ctypes.byref(r))
+            self.output_shapes.append([int(v) for v in shp[:r.value]])
+
+    def run_host(self, batches: Sequence[Sequence[np.ndarray | torch.Tensor]],
+                 outputs: Sequence[Sequence[np.ndarray | torch.Tensor]] | None = None):
+        """Runs full batches from host buffers (pinned for overlapped copies);
+        returns the host outputs, one list per batch."""
+        from .runtime import raise_for
+
+        def addr(t):
+            return t.ctypes.data if isinstance(t, np.ndarray) else t.data_ptr()
+
+        ins = [[np.ascontiguousarray(x, dtype=np.float32) if isinstance(x, np.ndarray) else x for x in b]
+               for b in batches]
+        for b in ins:
+            for t, (name, shape) in zip(b, self.input_specs):
+                if list(t.shape) != shape:
+                    raise ValueError(f"input {name}: expected shape {shape}, got {list(t.shape)}")
+        if outputs is None:
+            outputs = [[np.empty(s, np.float32) for s in self.output_shapes] for _ in ins]
+        flat_in = [addr(t) for b in ins for t in b]
+        flat_out = [addr(t) for b in outputs for t in b]
+        iarr = (ctypes.c_void_p * max(1, len(flat_in)))(*flat_in)
+        oarr = (ctypes.c_void_p * max(1, len(flat_out)))(*flat_out)
+        rc = self.lib.onnxb200_multi_run_host(self.ptr, len(ins), iarr, oarr)
+        if rc:
+            raise_for(rc, self.lib.onnxb200_multi_last_error(self.ptr).decode(errors="replace"))
+        return [list(o) for o in outputs]
+
+    def info(self) -> dict:
+        n = len(self.devices)
+        nd = ctypes.c_int()
+        b = ctypes.c_int64()
+        lo = (ctypes.c_int64 * n)()
+        ms = (ctypes.c_float * n)()
+        self.lib.onnxb200_multi_get_info(self.ptr, ctypes.byref(nd), ctypes.byref(b), lo, ms)
+        return {"n_devices": nd.value, "batch": b.value, "slice_begin": list(lo), "last_run_ms": list(ms)}
+
+    def close(self):
+        if getattr(self, "ptr", None):
+            self.lib.onnxb200_multi_destroy(self.ptr)
+            self.ptr = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

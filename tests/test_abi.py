@@ -219,3 +219,23 @@ def test_infer_shapes_errors(ob):
     assert C.lib().onnxb200_infer_shapes(None, 0, None, 0, None, 0, None, None, 0) == C.ERR_INVALID_ARGUMENT
     assert C.lib().onnxb200_infer_shapes(None, 0, None, 0, None, 0, ctypes.byref(n), None, 0) == C.OK
     assert n.value == 0
+
+
+def test_multi_build_argument_checks(ob):
+    """The multi-device build rejects bad arguments before touching a GPU."""
+    C = ob._capi
+    lib = C.lib()
+    p = ctypes.c_void_p()
+    err = ctypes.create_string_buffer(256)
+    assert lib.onnxb200_multi_build(None, 0, None, None, 0, None, 0, None, 0, None, 0, ctypes.byref(p), err,
+                                    256) == C.ERR_INVALID_ARGUMENT
+    with pytest.raises(ob.ValidationError, match="fewer images than devices"):
+        ob.MultiGraph([0, 1, 2], [{"op": "Relu", "inputs": ["X"], "outputs": ["Y"]}], {}, [("X", [2, 4])], ["Y"])
+    with pytest.raises(ob.ValidationError, match="listed twice"):
+        ob.MultiGraph([0, 0], [{"op": "Relu", "inputs": ["X"], "outputs": ["Y"]}], {}, [("X", [2, 4])], ["Y"])
+    with pytest.raises(ob.ValidationError, match="disagree"):
+        ob.MultiGraph([0], [{"op": "Add", "inputs": ["X", "Z"], "outputs": ["Y"]}], {},
+                      [("X", [2, 4]), ("Z", [3, 4])], ["Y"])
+    assert lib.onnxb200_multi_run_host(None, 1, None, None) == C.ERR_INVALID_ARGUMENT
+    assert lib.onnxb200_multi_destroy(None) == C.ERR_INVALID_ARGUMENT
+    assert lib.onnxb200_multi_last_error(None) == b"null multi-device graph"
