@@ -212,6 +212,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Programmatic dependent launch: the next kernel on the stream may start its
+  // CTAs (barrier set-up, TMEM allocation) on SMs this grid has left, and this
+  // grid's prologue above may have overlapped the previous kernel's tail; no
+  // global memory is touched before the previous grid has completed and its
+  // writes are visible.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 
   const int total_tiles = p.m_tiles * p.n_tiles * p.batches;
   // tile t -> (batch, m-tile, n-tile), n fastest: CTAs running together share
@@ -784,8 +791,19 @@ int launch3_t(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap& lo
   const int total = p.m_tiles * p.n_tiles * p.batches;
   const int grid = total < num_sms ? total : num_sms;
   if (grid <= 0) return 0;
-  igemm_tc3_kernel<PREC, BN, EG, NB><<<grid, kThreads, L::kBytes, st>>>(p, hi, lo, am, ym, rm);
-  return (int)cudaGetLastError();
+  // Launched as a programmatic dependent of the previous kernel on the stream
+  // (the kernel waits for it before touching global memory).
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = L::kBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return (int)cudaLaunchKernelEx(&cfg, igemm_tc3_kernel<PREC, BN, EG, NB>, p, hi, lo, am, ym, rm);
 }
 
 }  // namespace
