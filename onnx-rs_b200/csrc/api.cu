@@ -328,7 +328,7 @@ int conv_plan_exec_nhwc(onnxb200_handle* h, const onnxb200_conv_plan* p, const f
       const int er = encode_a_map(q, rows, &am);
       if (er) return set_error(h, ONNXB200_ERR_EXECUTION, "Conv: A tensor map encode failed: " + std::to_string(er));
     }
-    rc = igemm_launch(q, p->tm_hi, p->tm_lo, am, p->prec, p->bn, h->num_sms, h->stream);
+    rc = igemm_launch(q, p->tm_hi, p->tm_lo, am, am, p->prec, p->bn, h->num_sms, h->stream);
   } else {
     rc = conv_direct_launch(x, (int)d.n, (int)d.h, (int)d.w, (int)d.c, p->cs_in, p->w_oihw,
                             (int)d.c_out, (int)d.kh, (int)d.kw, (int)d.stride_h, (int)d.stride_w,
@@ -336,6 +336,146 @@ int conv_plan_exec_nhwc(onnxb200_handle* h, const onnxb200_conv_plan* p, const f
                             (int)d.group, (int)p->oh, (int)p->ow, p->scale, p->shift, res, relu, y,
                             h->stream);
   }
+  h->launches++;
+  if (rc) return cuda_check(h, (cudaError_t)rc, "Conv launch");
+  return ONNXB200_OK;
+}
+
+int conv_dual_plan_init(onnxb200_handle* h, const onnxb200_conv_desc* d1, int cs1, const float* w1,
+                        const ConvBranchBN& bn1, const onnxb200_conv_desc* d2, int cs2, const float* w2,
+                        const ConvBranchBN& bn2, onnxb200_conv_plan* p, void* scratch, size_t scratch_bytes,
+                        size_t* scratch_used) {
+  onnxb200_conv_desc r2;
+  int64_t oh2 = 0, ow2 = 0;
+  int rc = resolve_conv_desc(h, d1, &p->d, &p->oh, &p->ow);
+  if (rc) return rc;
+  rc = resolve_conv_desc(h, d2, &r2, &oh2, &ow2);
+  if (rc) return rc;
+  const onnxb200_conv_desc& a = p->d;
+  if (!dual_conv_supported(a, cs1, r2, cs2) || oh2 != p->oh || ow2 != p->ow || a.precision != r2.precision)
+    return set_error(h, ONNXB200_ERR_UNSUPPORTED, "Conv: these two convolutions cannot share one K loop");
+  if (!w1 || !w2) return set_error(h, ONNXB200_ERR_INVALID_ARGUMENT, "Conv: null weights");
+  const int CO = (int)a.c_out;
+  p->prec = a.precision;
+  p->cs_in = cs1;
+  p->use_tc = true;
+  p->pairs = false;
+  p->dual = true;
+  p->d2 = r2;
+  p->cs2 = cs2;
+  p->kb_split = (int)(a.c / 32);
+  p->K = (int)(a.c + r2.c);
+  p->kpad = p->K;
+  p->num_kb = p->K / 32;
+  const size_t esz = p->prec == kPrecBF16 ? 2 : 4;
+  const size_t wbytes = align_up((size_t)CO * p->kpad * esz);
+  size_t need = wbytes * (p->prec == kPrec3xTF32 ? 2 : 1);
+  const size_t off_s1 = need;
+  need += align_up(CO * sizeof(float));
+  const size_t off_s2 = need;
+  need += align_up(CO * sizeof(float));
+  const size_t off_t1 = need;
+  need += align_up(CO * sizeof(float));
+  const size_t off_t2 = need;
+  need += align_up(CO * sizeof(float));
+  p->weight_bytes = (int64_t)need;
+  if (!scratch && scratch_used) {
+    *scratch_used = need;
+    return ONNXB200_OK;
+  }
+  uint8_t* basep = nullptr;
+  if (scratch) {
+    if (need > scratch_bytes)
+      return set_error(h, ONNXB200_ERR_RESOURCE_EXHAUSTED, "Conv: scratch too small for packed weights");
+    basep = static_cast<uint8_t*>(scratch);
+    if (scratch_used) *scratch_used = need;
+  } else {
+    cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&basep), need);
+    if (e != cudaSuccess) return cuda_check(h, e, "conv plan allocation");
+  }
+  cudaStream_t st = h->stream;
+  p->w_hi = basep;
+  p->w_lo = p->prec == kPrec3xTF32 ? basep + wbytes : nullptr;
+  p->w_oihw = nullptr;
+  float* s1 = reinterpret_cast<float*>(basep + off_s1);
+  float* s2 = reinterpret_cast<float*>(basep + off_s2);
+  float* t1 = reinterpret_cast<float*>(basep + off_t1);
+  float* t2 = reinterpret_cast<float*>(basep + off_t2);
+  // each branch's BatchNormalization as scale / shift; the scales go into the
+  // packed weights, the shifts are added: y = (s1 W1) x1 + (s2 W2) x2 + t1 + t2
+  rc = bn_fold_launch(bn1.scale, bn1.bias, bn1.mean, bn1.var, bn1.conv_bias, bn1.eps, CO, s1, t1, st);
+  if (!rc) rc = bn_fold_launch(bn2.scale, bn2.bias, bn2.mean, bn2.var, bn2.conv_bias, bn2.eps, CO, s2, t2, st);
+  if (!rc) rc = pack_dual_b_launch(w1, s1, (int)a.c, w2, s2, (int)r2.c, CO, p->prec, p->w_hi, p->w_lo, st);
+  if (!rc) rc = vec_add_launch(t1, t2, t1, CO, st);
+  h->launches += 4;
+  if (rc) return cuda_check(h, (cudaError_t)rc, "two-source weight packing");
+  p->scale = nullptr;
+  p->shift = t1;
+  IgemmParams q{};
+  q.M = (int)(a.n * p->oh * p->ow);
+  q.Nc = CO;
+  q.batches = 1;
+  p->bn = igemm_pick_bn(q, p->prec, h->num_sms);
+  rc = encode_weight_map(h, &p->tm_hi, p->w_hi, CO, p->kpad, p->prec, p->bn);
+  if (rc) return rc;
+  return encode_weight_map(h, &p->tm_lo, p->w_lo ? p->w_lo : p->w_hi, CO, p->kpad, p->prec, p->bn);
+}
+
+bool dual_conv_supported(const onnxb200_conv_desc& a, int cs1, const onnxb200_conv_desc& b, int cs2) {
+  auto one_by_one = [](const onnxb200_conv_desc& d) {
+    return d.kh == 1 && d.kw == 1 && d.group == 1 && d.pad_top == 0 && d.pad_left == 0 && d.pad_bottom == 0 &&
+           d.pad_right == 0 && d.dil_h == 1 && d.dil_w == 1 && d.auto_pad == ONNXB200_AUTOPAD_NOTSET;
+  };
+  return one_by_one(a) && one_by_one(b) && a.stride_h == 1 && a.stride_w == 1 && b.stride_h == b.stride_w &&
+         b.stride_h <= 8 && a.c_out == b.c_out && a.n == b.n && cs1 == a.c && cs2 == b.c && a.c % 32 == 0 &&
+         b.c % 32 == 0 && a.c_out % 4 == 0 && a.precision != kPrecFP32 && a.precision == b.precision;
+}
+
+int conv_dual_exec_nhwc(onnxb200_handle* h, const onnxb200_conv_plan* p, const float* x1, const float* x2,
+                        float* y) {
+  const onnxb200_conv_desc& d = p->d;
+  if (!p->dual) return set_error(h, ONNXB200_ERR_INVALID_ARGUMENT, "Conv: not a two-source plan");
+  if (d.n == 0) return ONNXB200_OK;
+  IgemmParams q{};
+  q.x = x1;
+  q.Hin = (int)d.h;
+  q.Win = (int)d.w;
+  q.Cs = p->cs_in;
+  q.OH = (int)p->oh;
+  q.OW = (int)p->ow;
+  q.KW = 1;
+  q.sh = q.sw = 1;
+  q.dh = q.dw = 1;
+  q.M = (int)(d.n * p->oh * p->ow);
+  q.Nc = (int)d.c_out;
+  q.K = p->K;
+  q.num_kb = p->num_kb;
+  q.batches = 1;
+  q.y = y;
+  q.ldy = (int)d.c_out;
+  q.scale = p->scale;
+  q.shift = p->shift;
+  q.relu = (d.epilogue & ONNXB200_EPI_RELU) != 0;
+  q.status = h->d_status;
+  q.m_tiles = (q.M + 127) / 128;
+  q.n_tiles = (q.Nc + p->bn - 1) / p->bn;
+  q.a_mode = kALoadTma2d;
+  q.kb_split = p->kb_split;
+  q.x2 = x2;
+  q.H2 = (int)p->d2.h;
+  q.W2 = (int)p->d2.w;
+  q.Cs2 = p->cs2;
+  q.s2 = (int)p->d2.stride_h;
+  IgemmParams v = second_source_view(q);
+  q.a_mode2 = pick_a_mode(v, p->prec);
+  v.a_mode = q.a_mode2;
+  if (q.a_mode2 != kALoadTma2d && q.a_mode2 != kALoadIm2col)
+    return set_error(h, ONNXB200_ERR_UNSUPPORTED, "Conv: second source cannot be read by TMA");
+  CUtensorMap am{}, am2{};
+  int er = encode_a_map(q, (int)d.n * q.Hin * q.Win, &am);
+  if (!er) er = encode_a_map(v, q.a_mode2 == kALoadTma2d ? (int)d.n * q.H2 * q.W2 : (int)d.n, &am2);
+  if (er) return set_error(h, ONNXB200_ERR_EXECUTION, "Conv: A tensor map encode failed: " + std::to_string(er));
+  const int rc = igemm_launch(q, p->tm_hi, p->tm_lo, am, am2, p->prec, p->bn, h->num_sms, h->stream);
   h->launches++;
   if (rc) return cuda_check(h, (cudaError_t)rc, "Conv launch");
   return ONNXB200_OK;
@@ -384,7 +524,7 @@ int gemm_tc_run(onnxb200_handle* h, const GemmCall& c, const void* b_hi, const v
     const int er = encode_a_map(q, c.a_rows > 0 ? c.a_rows : c.M, &am);
     if (er) return set_error(h, ONNXB200_ERR_EXECUTION, "GEMM: A tensor map encode failed: " + std::to_string(er));
   }
-  rc = igemm_launch(q, thi, tlo, am, prec, bn, h->num_sms, h->stream);
+  rc = igemm_launch(q, thi, tlo, am, am, prec, bn, h->num_sms, h->stream);
   h->launches++;
   if (rc) return cuda_check(h, (cudaError_t)rc, "GEMM launch");
   return ONNXB200_OK;

@@ -502,6 +502,29 @@ extern "C" int onnxb200_graph_build(onnxb200_handle* h, const onnxb200_node* nod
     int residual = -1;        // tensor id
     int bias_add = -1;        // MatMul bias Add node
     int out = -1;
+    int dual_head = -1, dual_bn = -1;  // a merged second 1x1 Conv + BatchNormalization
+  };
+  // Conv descriptor of node `ci` (NHWC, the handle's precision); epilogue not set.
+  auto conv_desc_of = [&](int ci) {
+    const Node& nd = nodes[ci];
+    const GTensor& xt = g->tensors[nd.in[0]];
+    const auto& w = g->tensors[nd.in[1]].shape;
+    onnxb200_conv_desc d{};
+    d.n = xt.shape[0]; d.c = xt.shape[1]; d.h = xt.shape[2]; d.w = xt.shape[3];
+    d.c_out = w[0]; d.kh = w[2]; d.kw = w[3];
+    auto st = nd.getv("strides", {1, 1});
+    auto pd = nd.getv("pads", {0, 0, 0, 0});
+    auto dl = nd.getv("dilations", {1, 1});
+    d.stride_h = st[0]; d.stride_w = st.size() > 1 ? st[1] : st[0];
+    d.pad_top = pd[0]; d.pad_left = pd.size() > 1 ? pd[1] : 0;
+    d.pad_bottom = pd.size() > 2 ? pd[2] : d.pad_top; d.pad_right = pd.size() > 3 ? pd[3] : d.pad_left;
+    d.dil_h = dl[0]; d.dil_w = dl.size() > 1 ? dl[1] : dl[0];
+    d.group = nd.geti("group", 1);
+    const std::string ap = nd.gets("auto_pad", "NOTSET");
+    d.auto_pad = ap == "SAME_UPPER" ? 1 : ap == "SAME_LOWER" ? 2 : ap == "VALID" ? 3 : 0;
+    d.layout = ONNXB200_LAYOUT_NHWC;
+    d.precision = h->opts.precision;
+    return d;
   };
   std::vector<Fused> fused_at(n_nodes, Fused{-1, -1});
   for (int idx : order) {
@@ -572,6 +595,36 @@ extern "C" int onnxb200_graph_build(onnxb200_handle* h, const onnxb200_node* nod
     if (fused_at[f.last].head >= 0)
       return bail(ONNXB200_ERR_INVALID_GRAPH, "internal: two fused steps end at node " + nodes[f.last].op);
     fused_at[f.last] = f;
+  }
+  // Two convolutions added together -- Conv+BN -> Add(residual = Conv+BN) as in
+  // a bottleneck's last 1x1 and its projection shortcut -- become one
+  // two-source step when both are 1x1 convolutions the kernel can read from
+  // one K loop: the shortcut's output is then never written.
+  for (int idx : order) {
+    Fused& f = fused_at[idx];
+    if (f.head < 0 || nodes[f.head].op != "Conv" || f.bn < 0 || f.residual < 0) continue;
+    const int r = f.residual;
+    if (consumers[r] != 1 || g->tensors[r].is_output) continue;
+    int gi = -1;
+    for (int j = 0; j < n_nodes; ++j)
+      if (fused_at[j].head >= 0 && fused_at[j].out == r) gi = j;
+    if (gi < 0) continue;
+    const Fused& gf = fused_at[gi];
+    if (nodes[gf.head].op != "Conv" || gf.bn < 0 || gf.add >= 0 || gf.relu >= 0) continue;
+    const Node& n1 = nodes[f.head];
+    const Node& n2 = nodes[gf.head];
+    if ((n1.in.size() > 2 && n1.in[2] >= 0 && !is_const(n1.in[2])) ||
+        (n2.in.size() > 2 && n2.in[2] >= 0 && !is_const(n2.in[2])))
+      continue;
+    const onnxb200_conv_desc d1 = conv_desc_of(f.head), d2 = conv_desc_of(gf.head);
+    if (g->tensors[n1.in[0]].shape.size() != 4 || g->tensors[n2.in[0]].shape.size() != 4 ||
+        !dual_conv_supported(d1, (int)d1.c, d2, (int)d2.c))
+      continue;
+    f.dual_head = gf.head;
+    f.dual_bn = gf.bn;
+    f.residual = -1;
+    absorbed[gf.head] = 1;
+    fused_at[gi] = Fused{-1, -1};
   }
   for (int i = 0; i < n_nodes; ++i) g->n_fused += absorbed[i];
 
@@ -649,6 +702,8 @@ extern "C" int onnxb200_graph_build(onnxb200_handle* h, const onnxb200_node* nod
     int plan;
     onnxb200_conv_desc d;
     int x, w, b, bn;  // tensor ids / node
+    int dual_head, dual_bn;  // second branch (nodes) of a two-source step, or -1
+    int head;                // the Conv node
   };
   std::vector<PendingConv> pconv;
   struct PendingGemm {
@@ -674,23 +729,7 @@ extern "C" int onnxb200_graph_build(onnxb200_handle* h, const onnxb200_node* nod
     s.relu = f.relu >= 0;
     if (nd.op == "Conv") {
       const int x = nd.in[0];
-      const GTensor& xt = g->tensors[x];
-      const auto& w = g->tensors[nd.in[1]].shape;
-      onnxb200_conv_desc d{};
-      d.n = xt.shape[0]; d.c = xt.shape[1]; d.h = xt.shape[2]; d.w = xt.shape[3];
-      d.c_out = w[0]; d.kh = w[2]; d.kw = w[3];
-      auto st = nd.getv("strides", {1, 1});
-      auto pd = nd.getv("pads", {0, 0, 0, 0});
-      auto dl = nd.getv("dilations", {1, 1});
-      d.stride_h = st[0]; d.stride_w = st.size() > 1 ? st[1] : st[0];
-      d.pad_top = pd[0]; d.pad_left = pd.size() > 1 ? pd[1] : 0;
-      d.pad_bottom = pd.size() > 2 ? pd[2] : d.pad_top; d.pad_right = pd.size() > 3 ? pd[3] : d.pad_left;
-      d.dil_h = dl[0]; d.dil_w = dl.size() > 1 ? dl[1] : dl[0];
-      d.group = nd.geti("group", 1);
-      const std::string ap = nd.gets("auto_pad", "NOTSET");
-      d.auto_pad = ap == "SAME_UPPER" ? 1 : ap == "SAME_LOWER" ? 2 : ap == "VALID" ? 3 : 0;
-      d.layout = ONNXB200_LAYOUT_NHWC;
-      d.precision = h->opts.precision;
+      onnxb200_conv_desc d = conv_desc_of(f.head);
       const bool has_b = nd.in.size() > 2 && nd.in[2] >= 0;
       d.epilogue = (has_b ? ONNXB200_EPI_BIAS : 0) | (f.bn >= 0 ? ONNXB200_EPI_BN : 0) |
                    (f.residual >= 0 ? ONNXB200_EPI_RESIDUAL : 0) | (f.relu >= 0 ? ONNXB200_EPI_RELU : 0);
@@ -698,9 +737,10 @@ extern "C" int onnxb200_graph_build(onnxb200_handle* h, const onnxb200_node* nod
       s.type = kConv;
       s.in = {x};
       if (f.residual >= 0) s.in.push_back(f.residual);
+      if (f.dual_head >= 0) s.in.push_back(nodes[f.dual_head].in[0]);
       s.conv = (int)g->plans.size();
       g->plans.emplace_back();
-      pconv.push_back({s.conv, d, x, nd.in[1], has_b ? nd.in[2] : -1, f.bn});
+      pconv.push_back({s.conv, d, x, nd.in[1], has_b ? nd.in[2] : -1, f.bn, f.dual_head, f.dual_bn, f.head});
     } else if (nd.op == "MaxPool") {
       auto k = nd.getv("kernel_shape", {});
       auto st = nd.getv("strides", {1, 1});
@@ -925,20 +965,41 @@ extern "C" int onnxb200_graph_build(onnxb200_handle* h, const onnxb200_node* nod
     }
   auto dptr = [&](int t) -> float* { return reinterpret_cast<float*>(g->init + g->tensors[t].init_off); };
 
-  // conv plans: size, then carve from one weight arena
-  std::vector<size_t> plan_off(pconv.size());
-  size_t wtotal = 0;
-  for (size_t i = 0; i < pconv.size(); ++i) {
-    const PendingConv& pc = pconv[i];
+  // conv plans: size, then carve from one weight arena.  scratch == nullptr:
+  // size query into *used.
+  auto init_plan = [&](const PendingConv& pc, void* scratch, size_t bytes, size_t* used) -> int {
     const GTensor& xt = g->tensors[pc.x];
-    size_t need = 0;
+    const int cs = xt.cs ? xt.cs : (int)xt.shape[1];
+    auto branch_bn = [&](int bn_node, int conv_node) {
+      ConvBranchBN b;
+      const Node& bn = nodes[bn_node];
+      b.scale = dptr(bn.in[1]); b.bias = dptr(bn.in[2]); b.mean = dptr(bn.in[3]); b.var = dptr(bn.in[4]);
+      b.eps = bn.getf("epsilon", 1e-5f);
+      const Node& cn = nodes[conv_node];
+      if (cn.in.size() > 2 && cn.in[2] >= 0) b.conv_bias = dptr(cn.in[2]);
+      return b;
+    };
+    if (pc.dual_head >= 0) {
+      const Node& c2 = nodes[pc.dual_head];
+      const GTensor& x2 = g->tensors[c2.in[0]];
+      const onnxb200_conv_desc d2 = conv_desc_of(pc.dual_head);
+      return conv_dual_plan_init(h, &pc.d, cs, dptr(pc.w), branch_bn(pc.bn, pc.head), &d2,
+                                 x2.cs ? x2.cs : (int)x2.shape[1], dptr(c2.in[1]), branch_bn(pc.dual_bn, pc.dual_head),
+                                 &g->plans[pc.plan], scratch, bytes, used);
+    }
     const float *qb = pc.b >= 0 ? dptr(pc.b) : nullptr, *q1 = nullptr, *q2 = nullptr, *q3 = nullptr, *q4 = nullptr;
     if (pc.bn >= 0) {
       const Node& bn = nodes[pc.bn];
       q1 = dptr(bn.in[1]); q2 = dptr(bn.in[2]); q3 = dptr(bn.in[3]); q4 = dptr(bn.in[4]);
     }
-    int rc = conv_plan_init(h, &pc.d, xt.cs ? xt.cs : (int)xt.shape[1], dptr(pc.w), qb, q1, q2, q3, q4,
-                            &g->plans[pc.plan], nullptr, 0, &need);
+    return conv_plan_init(h, &pc.d, cs, dptr(pc.w), qb, q1, q2, q3, q4, &g->plans[pc.plan], scratch, bytes, used);
+  };
+  std::vector<size_t> plan_off(pconv.size());
+  size_t wtotal = 0;
+  for (size_t i = 0; i < pconv.size(); ++i) {
+    const PendingConv& pc = pconv[i];
+    size_t need = 0;
+    int rc = init_plan(pc, nullptr, 0, &need);
     if (rc) { destroy_graph(g); return rc; }
     plan_off[i] = wtotal;
     wtotal += align_up(need);
@@ -959,17 +1020,8 @@ extern "C" int onnxb200_graph_build(onnxb200_handle* h, const onnxb200_node* nod
     if (e != cudaSuccess) return bail(ONNXB200_ERR_RESOURCE_EXHAUSTED, "graph: weight allocation failed");
   }
   for (size_t i = 0; i < pconv.size(); ++i) {
-    const PendingConv& pc = pconv[i];
-    const GTensor& xt = g->tensors[pc.x];
-    const float* bias = pc.b >= 0 ? dptr(pc.b) : nullptr;
-    const float *bs = nullptr, *bb = nullptr, *bm = nullptr, *bv = nullptr;
-    if (pc.bn >= 0) {
-      const Node& bn = nodes[pc.bn];
-      bs = dptr(bn.in[1]); bb = dptr(bn.in[2]); bm = dptr(bn.in[3]); bv = dptr(bn.in[4]);
-    }
     size_t used = 0;
-    int rc = conv_plan_init(h, &pc.d, xt.cs ? xt.cs : (int)xt.shape[1], dptr(pc.w), bias, bs, bb, bm, bv,
-                            &g->plans[pc.plan], g->weights + plan_off[i], wtotal - plan_off[i], &used);
+    int rc = init_plan(pconv[i], g->weights + plan_off[i], wtotal - plan_off[i], &used);
     if (rc) { destroy_graph(g); return rc; }
   }
   for (size_t i = 0; i < pgemm.size(); ++i) {
@@ -1105,7 +1157,10 @@ static int run_steps(onnxb200_graph* g, const float* const* uin, float* const* u
       }
       case kConv: {
         const onnxb200_conv_plan& p = g->plans[s.conv];
-        rc = conv_plan_exec_nhwc(h, &p, T(s.in[0]), s.in.size() > 1 ? T(s.in[1]) : nullptr, T(s.out));
+        if (p.dual)
+          rc = conv_dual_exec_nhwc(h, &p, T(s.in[0]), T(s.in[1]), T(s.out));
+        else
+          rc = conv_plan_exec_nhwc(h, &p, T(s.in[0]), s.in.size() > 1 ? T(s.in[1]) : nullptr, T(s.out));
         if (rc) return rc;
         break;
       }
@@ -1234,6 +1289,10 @@ static void step_work(const onnxb200_graph* g, const Step& s, int* kind, double*
       *kind = p.use_tc ? ONNXB200_STEP_CONV_TC : ONNXB200_STEP_CONV_DIRECT;
       *flops = 2.0 * d.n * p.oh * p.ow * d.c_out * (double)(d.c / d.group) * d.kh * d.kw;
       *bytes += (double)d.c_out * (d.c / d.group) * d.kh * d.kw * 4.0;
+      if (p.dual) {  // the second 1x1 branch
+        *flops += 2.0 * d.n * p.oh * p.ow * d.c_out * (double)p.d2.c;
+        *bytes += (double)d.c_out * p.d2.c * 4.0;
+      }
       break;
     }
     case kGemm: {

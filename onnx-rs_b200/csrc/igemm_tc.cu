@@ -33,8 +33,25 @@ int igemm_pick_bn(const IgemmParams& p, int precision, int num_sms) {
   return 128;
 }
 
+IgemmParams second_source_view(const IgemmParams& p) {
+  IgemmParams v = p;
+  v.x = p.x2;
+  v.Hin = p.H2;
+  v.Win = p.W2;
+  v.Cs = p.Cs2;
+  v.KW = 1;
+  v.sh = v.sw = p.s2;
+  v.ph = v.pw = 0;
+  v.dh = v.dw = 1;
+  v.K = p.Cs2;
+  v.a_mode = p.a_mode2;
+  v.kb_split = 0;
+  return v;
+}
+
 int igemm_launch(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap& lo,
-                 const CUtensorMap& am, int precision, int bn, int num_sms, cudaStream_t st) {
+                 const CUtensorMap& am, const CUtensorMap& am2, int precision, int bn, int num_sms,
+                 cudaStream_t st) {
   if (p.a_mode != kALoadGather &&
       (p.a_mode == kALoadIm2colTaps ? ((p.Cs != 4 && p.Cs != 8 && p.Cs != 16) || p.K % p.Cs != 0)
        : p.a_mode == kALoadIm2col   ? p.Cs % 32 != 0
@@ -47,8 +64,16 @@ int igemm_launch(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap&
       (p.shift && mis(p.shift)) || p.Cs % 4 || p.Nc % 4 || p.ldy % 4 || (p.res && p.ldr % 4) ||
       p.y_bstride % 4 || p.num_kb <= 0 || (p.batches > 1 && !p.a_off && p.M % 4))
     return (int)cudaErrorMisalignedAddress;
+  // two sources: source 1 a [pixels][Cs] matrix of whole k-blocks, source 2 a
+  // 1x1 convolution of whole k-blocks at the same output pixels
+  if (p.kb_split &&
+      (p.a_mode != kALoadTma2d || p.Cs != p.kb_split * 32 || p.batches != 1 || p.a_off || !p.x2 ||
+       mis(p.x2) || p.Cs2 % 32 || p.s2 < 1 || p.num_kb != p.kb_split + p.Cs2 / 32 ||
+       (p.a_mode2 != kALoadTma2d && p.a_mode2 != kALoadIm2col) ||
+       (p.a_mode2 == kALoadTma2d && (p.s2 != 1 || p.H2 != p.OH || p.W2 != p.OW))))
+    return (int)cudaErrorInvalidValue;
   if (precision == kPrec3xTF32 || precision == kPrecTF32 || precision == kPrecBF16)
-    return igemm3_launch(p, hi, lo, am, precision, bn, num_sms, st);
+    return igemm3_launch(p, hi, lo, am, am2, precision, bn, num_sms, st);
   return (int)cudaErrorInvalidValue;
 }
 

@@ -152,7 +152,8 @@ template <int PREC, int BN, int EG, int NB>
 __global__ void __launch_bounds__(kThreads, 1)
     igemm_tc3_kernel(const __grid_constant__ IgemmParams p, const __grid_constant__ CUtensorMap tm_hi,
                      const __grid_constant__ CUtensorMap tm_lo, const __grid_constant__ CUtensorMap tm_a,
-                     const __grid_constant__ CUtensorMap tm_y, const __grid_constant__ CUtensorMap tm_res) {
+                     const __grid_constant__ CUtensorMap tm_a2, const __grid_constant__ CUtensorMap tm_y,
+                     const __grid_constant__ CUtensorMap tm_res) {
   using L = Layout<PREC, BN, EG, NB>;
   constexpr int kEG = EG;
   constexpr int kEpiTile = L::kEpiTile;
@@ -201,6 +202,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tmap(&tm_hi);
     if (L::kSplit) prefetch_tmap(&tm_lo);
     if (p.a_mode != kALoadGather) prefetch_tmap(&tm_a);
+    if (p.kb_split) prefetch_tmap(&tm_a2);
     prefetch_tmap(&tm_y);
     if (p.res) prefetch_tmap(&tm_res);
   }
@@ -284,9 +286,27 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           const int brow = nt * BN + (p.b_row ? p.b_row[b] : 0);
+          // second source (two-source problems): 32 channels of the 1x1 input
+          // x2 at the output pixels of this tile
+          const bool src2 = p.kb_split && kb >= p.kb_split;
+          int b_x = 0, b_y = 0, b_n = 0;
+          if (src2 && p.a_mode2 != kALoadTma2d) {
+            const int m0 = mt * kBM;
+            b_n = m0 / OHW;
+            const int rem = m0 - b_n * OHW;
+            const int oh0 = rem / p.OW;
+            b_x = (rem - oh0 * p.OW) * p.s2;
+            b_y = oh0 * p.s2;
+          }
           if (!mbar_wait(s1_empty(s), ((item / S1) & 1) ^ 1, abort_flag, p.status)) break;
           mbar_arrive_expect_tx(s1_full(s), tx_bytes);
-          if (p.a_mode == kALoadTma2d) {
+          if (src2) {
+            const int k2 = (kb - p.kb_split) * kBK;
+            if (p.a_mode2 == kALoadTma2d)
+              tma_load_2d(dst, &tm_a2, k2, mt * kBM, s1_full(s));
+            else
+              tma_load_im2col_4d(dst, &tm_a2, k2, b_x, b_y, b_n, 0, 0, s1_full(s));
+          } else if (p.a_mode == kALoadTma2d) {
             if (a_taps) tma_load_2d(dst, &tm_a, c0, a_r0, s1_full(s));
           } else {
 #pragma unroll
@@ -772,7 +792,7 @@ int encode_out_map(const float* base, int cols, int rows, int batches, int ld, l
 
 template <int PREC, int BN, int EG, int NB>
 int launch3_t(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap& lo,
-              const CUtensorMap& am, int num_sms, cudaStream_t st) {
+              const CUtensorMap& am, const CUtensorMap& am2, int num_sms, cudaStream_t st) {
   using L = Layout<PREC, BN, EG, NB>;
   static bool attr_set = false;
   if (!attr_set) {
@@ -803,7 +823,7 @@ int launch3_t(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap& lo
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return (int)cudaLaunchKernelEx(&cfg, igemm_tc3_kernel<PREC, BN, EG, NB>, p, hi, lo, am, ym, rm);
+  return (int)cudaLaunchKernelEx(&cfg, igemm_tc3_kernel<PREC, BN, EG, NB>, p, hi, lo, am, am2, ym, rm);
 }
 
 }  // namespace
@@ -812,7 +832,8 @@ constexpr int kLongK = 16;  // k-blocks (K >= 512)
 constexpr int kShortK = 2;  // k-blocks (K <= 64)
 
 int igemm3_launch(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap& lo,
-                  const CUtensorMap& am, int precision, int bn, int num_sms, cudaStream_t st) {
+                  const CUtensorMap& am, const CUtensorMap& am2, int precision, int bn, int num_sms,
+                  cudaStream_t st) {
   // 3xTF32, BN = 128: 16-column epilogue groups buy a fourth operand stage,
   // worth it once the K loop of a tile is long (short-K layers are bound by
   // their epilogue, which 32-column groups store faster)
@@ -820,25 +841,25 @@ int igemm3_launch(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap
   // buffers (more stores and residual loads in flight) instead of operand stages.
   const bool short_k = p.num_kb <= kShortK;
   if (precision == kPrec3xTF32 && bn == 64)
-    return short_k ? launch3_t<kPrec3xTF32, 64, 32, 4>(p, hi, lo, am, num_sms, st)
-                   : launch3_t<kPrec3xTF32, 64, 32, 2>(p, hi, lo, am, num_sms, st);
+    return short_k ? launch3_t<kPrec3xTF32, 64, 32, 4>(p, hi, lo, am, am2, num_sms, st)
+                   : launch3_t<kPrec3xTF32, 64, 32, 2>(p, hi, lo, am, am2, num_sms, st);
   if (precision == kPrec3xTF32 && bn == 128)
-    return p.num_kb >= kLongK ? launch3_t<kPrec3xTF32, 128, 16, 2>(p, hi, lo, am, num_sms, st)
-           : short_k          ? launch3_t<kPrec3xTF32, 128, 32, 4>(p, hi, lo, am, num_sms, st)
-                              : launch3_t<kPrec3xTF32, 128, 32, 2>(p, hi, lo, am, num_sms, st);
+    return p.num_kb >= kLongK ? launch3_t<kPrec3xTF32, 128, 16, 2>(p, hi, lo, am, am2, num_sms, st)
+           : short_k          ? launch3_t<kPrec3xTF32, 128, 32, 4>(p, hi, lo, am, am2, num_sms, st)
+                              : launch3_t<kPrec3xTF32, 128, 32, 2>(p, hi, lo, am, am2, num_sms, st);
   if (precision == kPrecTF32 && bn == 64)
-    return short_k ? launch3_t<kPrecTF32, 64, 32, 4>(p, hi, lo, am, num_sms, st)
-                   : launch3_t<kPrecTF32, 64, 32, 2>(p, hi, lo, am, num_sms, st);
+    return short_k ? launch3_t<kPrecTF32, 64, 32, 4>(p, hi, lo, am, am2, num_sms, st)
+                   : launch3_t<kPrecTF32, 64, 32, 2>(p, hi, lo, am, am2, num_sms, st);
   if (precision == kPrecTF32 && bn == 128)
-    return short_k ? launch3_t<kPrecTF32, 128, 32, 4>(p, hi, lo, am, num_sms, st)
-                   : launch3_t<kPrecTF32, 128, 32, 2>(p, hi, lo, am, num_sms, st);
-  if (precision == kPrecTF32 && bn == 256) return launch3_t<kPrecTF32, 256, 32, 2>(p, hi, lo, am, num_sms, st);
+    return short_k ? launch3_t<kPrecTF32, 128, 32, 4>(p, hi, lo, am, am2, num_sms, st)
+                   : launch3_t<kPrecTF32, 128, 32, 2>(p, hi, lo, am, am2, num_sms, st);
+  if (precision == kPrecTF32 && bn == 256) return launch3_t<kPrecTF32, 256, 32, 2>(p, hi, lo, am, am2, num_sms, st);
   if (precision == kPrecBF16 && bn == 64)
-    return short_k ? launch3_t<kPrecBF16, 64, 32, 4>(p, hi, lo, am, num_sms, st)
-                   : launch3_t<kPrecBF16, 64, 32, 2>(p, hi, lo, am, num_sms, st);
+    return short_k ? launch3_t<kPrecBF16, 64, 32, 4>(p, hi, lo, am, am2, num_sms, st)
+                   : launch3_t<kPrecBF16, 64, 32, 2>(p, hi, lo, am, am2, num_sms, st);
   if (precision == kPrecBF16 && bn == 128)
-    return short_k ? launch3_t<kPrecBF16, 128, 32, 4>(p, hi, lo, am, num_sms, st)
-                   : launch3_t<kPrecBF16, 128, 32, 2>(p, hi, lo, am, num_sms, st);
+    return short_k ? launch3_t<kPrecBF16, 128, 32, 4>(p, hi, lo, am, am2, num_sms, st)
+                   : launch3_t<kPrecBF16, 128, 32, 2>(p, hi, lo, am, am2, num_sms, st);
   return (int)cudaErrorInvalidValue;
 }
 

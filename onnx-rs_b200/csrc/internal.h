@@ -45,6 +45,14 @@ struct onnxb200_conv_plan {
   // input is read as [N][H][W/2][8] and the convolution runs with stride 1 over
   // ceil((KW + pw%2)/2) pair taps -- the same memory, half the TMA box rows.
   bool pairs = false;
+  // Two sources (conv_dual_plan_init): a 1x1 stride-1 convolution of x (this
+  // descriptor) plus a 1x1 convolution of x2 (d2, stride d2.stride_h) at the
+  // same output pixels, weights packed side by side along K with each branch's
+  // folded BatchNormalization scale, shift = both branches' shifts.
+  bool dual = false;
+  onnxb200_conv_desc d2{};
+  int cs2 = 0;
+  int kb_split = 0;
 };
 
 namespace ob2 {
@@ -70,6 +78,28 @@ int conv_plan_init(onnxb200_handle* h, const onnxb200_conv_desc* d, int cs_in, c
                    const float* bn_mean, const float* bn_var, onnxb200_conv_plan* p,
                    void* scratch, size_t scratch_bytes, size_t* scratch_used);
 void conv_plan_free(onnxb200_conv_plan* p);
+
+// BatchNormalization of one branch of a two-source convolution (all device
+// pointers; conv_bias may be null).
+struct ConvBranchBN {
+  const float* scale = nullptr;
+  const float* bias = nullptr;
+  const float* mean = nullptr;
+  const float* var = nullptr;
+  const float* conv_bias = nullptr;
+  float eps = 1e-5f;
+};
+// Whether y = BN1(conv1(x1)) + BN2(conv2(x2)) can run as one two-source
+// problem: both 1x1 pad-0 convolutions with channel counts that are multiples
+// of 32 and no channel padding, conv1 of stride 1, the same output shape and a
+// tensor-core precision.
+bool dual_conv_supported(const onnxb200_conv_desc& d1, int cs1, const onnxb200_conv_desc& d2, int cs2);
+int conv_dual_plan_init(onnxb200_handle* h, const onnxb200_conv_desc* d1, int cs1, const float* w1,
+                        const ConvBranchBN& bn1, const onnxb200_conv_desc* d2, int cs2, const float* w2,
+                        const ConvBranchBN& bn2, onnxb200_conv_plan* p, void* scratch, size_t scratch_bytes,
+                        size_t* scratch_used);
+int conv_dual_exec_nhwc(onnxb200_handle* h, const onnxb200_conv_plan* p, const float* x1, const float* x2,
+                        float* y);
 
 // Runs a plan on NHWC buffers (x channel stride p->cs_in, y / residual stride C_out).
 int conv_plan_exec_nhwc(onnxb200_handle* h, const onnxb200_conv_plan* p, const float* x,

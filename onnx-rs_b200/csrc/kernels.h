@@ -44,6 +44,16 @@ struct IgemmParams {
   // TMA im2col of 32 / Cs whole filter taps per k-block (Cs = 4, 8 or 16, e.g.
   // an RGB stem).
   int a_mode;
+  // Second A source (0 = none): k-blocks kb >= kb_split read a 1x1, pad-0
+  // convolution of stride s2 over another NHWC tensor x2 ([N][H2][W2][Cs2])
+  // at the same output pixels, so that two convolutions whose outputs are
+  // added (a bottleneck's last 1x1 and its projection shortcut) share one
+  // K loop and one accumulator; B holds both weight matrices back to back
+  // along K.  Source 1 is then a kALoadTma2d problem with K1 = kb_split * 32.
+  int kb_split;
+  const float* x2;
+  int H2, W2, Cs2, s2;
+  int a_mode2;             // kALoadTma2d (stride 1) or kALoadIm2col
 };
 
 enum ALoadMode { kALoadGather = 0, kALoadTma2d = 1, kALoadIm2col = 2, kALoadIm2colTaps = 3 };
@@ -59,15 +69,22 @@ int pick_a_mode(const IgemmParams& p, int precision);
 // Picks BN (64/128/256) for a problem; returned value is what launch uses.
 int igemm_pick_bn(const IgemmParams& p, int precision, int num_sms);
 
+// The view of the second A source of a two-source problem as a single-source
+// problem (x2 and its geometry), for encode_a_map.
+IgemmParams second_source_view(const IgemmParams& p);
+
 // Launches the tcgen05 kernel.  tm_hi / tm_lo are TMA maps over the packed
-// weights (tm_lo is only read in 3xTF32 mode).  Returns a cudaError_t.
+// weights (tm_lo is only read in 3xTF32 mode); tm_a2 is the map of the second
+// A source (ignored unless p.kb_split > 0).  Returns a cudaError_t.
 int igemm_launch(const IgemmParams& p, const CUtensorMap& tm_hi, const CUtensorMap& tm_lo,
-                 const CUtensorMap& tm_a, int precision, int bn, int num_sms, cudaStream_t stream);
+                 const CUtensorMap& tm_a, const CUtensorMap& tm_a2, int precision, int bn, int num_sms,
+                 cudaStream_t stream);
 
 // The tcgen05 kernel (3xTF32 / TF32 / BF16 operands from fp32 activations,
 // k-blocks of 32) behind igemm_launch.
 int igemm3_launch(const IgemmParams& p, const CUtensorMap& tm_hi, const CUtensorMap& tm_lo,
-                  const CUtensorMap& tm_a, int precision, int bn, int num_sms, cudaStream_t stream);
+                  const CUtensorMap& tm_a, const CUtensorMap& tm_a2, int precision, int bn, int num_sms,
+                  cudaStream_t stream);
 
 // K elements per k-block of the kernel used for a precision (p.num_kb = Kpad / this).
 inline int igemm_block_k(int) { return 32; }
@@ -105,6 +122,16 @@ int gemm_simt_launch(const float* a, const float* b, int batches, const long lon
 int pack_b_launch(const float* src, int rows, int K, int Kpad, int Cs, int Creal, int rpg,
                   long long gs, long long rs, long long ts, long long cs, int precision,
                   void* hi, void* lo, cudaStream_t stream, int pair_kw = 0, int pair_odd = 0);
+
+// Packs two 1x1 convolutions' weights ([rows][K1] and [rows][K2], row-major)
+// side by side along K, each row scaled by its branch's per-row factor (the
+// folded BatchNormalization scale; null = 1): the B operand of a two-source
+// problem.  Kpad = K1 + K2 (both multiples of 32).  hi / lo as pack_b_launch.
+int pack_dual_b_launch(const float* w1, const float* scale1, int K1, const float* w2, const float* scale2,
+                       int K2, int rows, int precision, void* hi, void* lo, cudaStream_t stream);
+
+// y[i] = a[i] + b[i] (n floats; the two branches' folded shifts).
+int vec_add_launch(const float* a, const float* b, float* y, int n, cudaStream_t stream);
 
 // NCHW -> NHWC with channel padding to Cp (zero-filled), and NHWC -> NCHW.
 int nchw_to_nhwc_launch(const float* x, int N, int C, int H, int W, int Cp, float* y,

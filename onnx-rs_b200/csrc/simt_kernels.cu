@@ -320,6 +320,50 @@ int pack_b_launch(const float* src, int rows, int K, int Kpad, int Cs, int Creal
   return (int)cudaGetLastError();
 }
 
+// Two 1x1 convolutions' weights side by side along K, each row scaled by its
+// branch's factor; split like pack_b_kernel.
+__global__ void pack_dual_b_kernel(const float* __restrict__ w1, const float* __restrict__ s1, int K1,
+                                   const float* __restrict__ w2, const float* __restrict__ s2, int K2,
+                                   int rows, int prec, void* hi, void* lo) {
+  const int Kp = K1 + K2;
+  const long long total = (long long)rows * Kp;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int row = (int)(i / Kp);
+    const int k = (int)(i % Kp);
+    const float v = k < K1 ? w1[(long long)row * K1 + k] * (s1 ? s1[row] : 1.f)
+                           : w2[(long long)row * K2 + (k - K1)] * (s2 ? s2[row] : 1.f);
+    if (prec == kPrecBF16) {
+      reinterpret_cast<__nv_bfloat16*>(hi)[i] = __float2bfloat16_rn(v);
+    } else if (prec == kPrec3xTF32) {
+      const float h = tf32_trunc(v);
+      reinterpret_cast<float*>(hi)[i] = h;
+      reinterpret_cast<float*>(lo)[i] = to_tf32(v - h);
+    } else {
+      reinterpret_cast<float*>(hi)[i] = to_tf32(v);
+    }
+  }
+}
+
+int pack_dual_b_launch(const float* w1, const float* s1, int K1, const float* w2, const float* s2, int K2,
+                       int rows, int prec, void* hi, void* lo, cudaStream_t st) {
+  const long long total = (long long)rows * (K1 + K2);
+  if (total == 0) return 0;
+  pack_dual_b_kernel<<<grid_for(total, kBlock), kBlock, 0, st>>>(w1, s1, K1, w2, s2, K2, rows, prec, hi, lo);
+  return (int)cudaGetLastError();
+}
+
+__global__ void vec_add_kernel(const float* a, const float* b, float* y, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) y[i] = a[i] + b[i];
+}
+
+int vec_add_launch(const float* a, const float* b, float* y, int n, cudaStream_t st) {
+  if (n == 0) return 0;
+  vec_add_kernel<<<(n + 255) / 256, 256, 0, st>>>(a, b, y, n);
+  return (int)cudaGetLastError();
+}
+
 // ------------------------------------------------------------------ layout repacks
 // 32x32 tiles through shared memory: NCHW [n][c][hw] <-> NHWC [n][hw][c].
 __global__ void nchw_to_nhwc_kernel(const float* __restrict__ x, int C, int HW, int Cp,

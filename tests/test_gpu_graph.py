@@ -207,3 +207,59 @@ def test_resnet50_fast_modes(ob, oracle, r50_b256, r50_b256_ref64, precision):
     check_logits_fast(y.cpu().numpy(), r50_b256_ref64, f"resnet50 b256/{precision}")
     g.close()
     h.close()
+
+
+def _projection_block(stride, cin, cmid, cout, hw, seed):
+    """x -> Conv1x1(cin->cmid, stride)+BN+Relu -> Conv1x1(cmid->cout)+BN, plus the
+    shortcut Conv1x1(cin->cout, stride)+BN of x, Add, Relu: the tail of a
+    ResNet-50 bottleneck with a projection shortcut."""
+    rng = np.random.default_rng(seed)
+    inits = {}
+
+    def conv_bn(x, ci, co, st, name, relu):
+        inits[name + "_W"] = (rng.standard_normal((co, ci, 1, 1)) * np.sqrt(2.0 / ci)).astype(np.float32)
+        inits[name + "_g"] = rng.uniform(0.5, 1.5, co).astype(np.float32)
+        inits[name + "_b"] = rng.uniform(-0.2, 0.2, co).astype(np.float32)
+        inits[name + "_m"] = rng.normal(0, 0.1, co).astype(np.float32)
+        inits[name + "_v"] = rng.uniform(0.5, 1.5, co).astype(np.float32)
+        nodes = [{"op": "Conv", "inputs": [x, name + "_W"], "outputs": [name + "_c"],
+                  "attrs": {"kernel_shape": [1, 1], "strides": [st, st], "pads": [0, 0, 0, 0]}},
+                 {"op": "BatchNormalization", "inputs": [name + "_c", name + "_g", name + "_b", name + "_m",
+                                                         name + "_v"], "outputs": [name + "_bn"],
+                  "attrs": {"epsilon": 1e-5}}]
+        out = name + "_bn"
+        if relu:
+            nodes.append({"op": "Relu", "inputs": [out], "outputs": [name + "_r"]})
+            out = name + "_r"
+        return nodes, out
+
+    n1, y = conv_bn("X", cin, cmid, stride, "a", True)
+    n2, y = conv_bn(y, cmid, cout, 1, "b", False)
+    n3, sc = conv_bn("X", cin, cout, stride, "p", False)
+    nodes = n1 + n2 + n3 + [{"op": "Add", "inputs": [y, sc], "outputs": ["s"]},
+                            {"op": "Relu", "inputs": ["s"], "outputs": ["Y"]}]
+    return nodes, inits
+
+
+@pytest.mark.parametrize("stride", [1, 2])
+@pytest.mark.parametrize("precision", ["3xtf32", "tf32", "bf16"])
+def test_two_source_conv_graph(ob, oracle, stride, precision):
+    """A block whose last 1x1 Conv+BN and projection shortcut Conv+BN are added:
+    the graph runs both convolutions as one two-source step (one kernel, the
+    shortcut's output never written) and matches the unfused oracle."""
+    nodes, inits = _projection_block(stride, 64, 32, 128, 14, 21 + stride)
+    x = np.random.default_rng(5).standard_normal((3, 64, 14, 14)).astype(np.float32)
+    ref = oracle.run_graph(nodes, inits, {"X": x}, ["Y"])["Y"]
+    h = ob.Handle(0, precision=precision)
+    g = ob.Graph(h, nodes, inits, [("X", list(x.shape))], ["Y"])
+    st = g.stats()
+    assert st["n_steps"] == 2, st  # conv a, then the merged conv b + shortcut
+    y = g.run([torch.from_numpy(x).cuda()])[0]
+    h.synchronize()
+    if precision == "3xtf32":
+        from conftest import assert_close
+        assert_close(y.cpu().numpy(), ref, 1e-5, 1e-4, f"two-source block s{stride}")
+    else:  # two chained layers of 7- / 10-bit operands: the fast-mode bar, per image
+        check_logits_fast(y.cpu().numpy(), ref, f"two-source block s{stride}/{precision}")
+    g.close()
+    h.close()
