@@ -303,6 +303,7 @@ typedef struct onnxb200_graph_stats {
   int64_t arena_bytes;   /* activation arena (planned, one allocation) */
   int64_t weight_bytes;  /* packed weights */
   int captured;          /* 1 if runs replay a CUDA graph */
+  int bf16_tensors;      /* activations stored as bf16 (BF16 precision) */
 } onnxb200_graph_stats;
 
 typedef struct onnxb200_graph onnxb200_graph;

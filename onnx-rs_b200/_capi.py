@@ -95,7 +95,7 @@ STEP_KINDS = {1: "conv_tc", 2: "conv_direct", 3: "gemm", 4: "maxpool", 5: "gap",
 class GraphStats(ctypes.Structure):
     _fields_ = [("n_nodes_in", ctypes.c_int), ("n_steps", ctypes.c_int), ("n_fused", ctypes.c_int),
                 ("kernels_per_run", ctypes.c_int64), ("arena_bytes", ctypes.c_int64),
-                ("weight_bytes", ctypes.c_int64), ("captured", ctypes.c_int)]
+                ("weight_bytes", ctypes.c_int64), ("captured", ctypes.c_int), ("bf16_tensors", ctypes.c_int)]
 
 
 class ModelInfo(ctypes.Structure):

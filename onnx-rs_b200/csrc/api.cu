@@ -72,19 +72,19 @@ int ensure_workspace(onnxb200_handle* h, size_t bytes) {
 }
 
 int encode_weight_map(onnxb200_handle* h, CUtensorMap* map, const void* base, int rows, int kpad,
-                      int prec, int bn) {
+                      int prec, int bn, int bk) {
   EncodeTiledFn fn = get_encode_fn();
   if (!fn) return set_error(h, ONNXB200_ERR_EXECUTION, "cuTensorMapEncodeTiled unavailable");
   const int esz = prec == kPrecBF16 ? 2 : 4;
   cuuint64_t dims[2] = {(cuuint64_t)kpad, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)kpad * esz};
-  // one k-block of a weight row = 32 elements: 128 bytes of fp32 (128-byte
-  // swizzle) or 64 bytes of bf16 (64-byte swizzle)
-  cuuint32_t box[2] = {32u, (cuuint32_t)bn};
+  // one k-block of a weight row = bk elements: 128 bytes of fp32 or (bk = 64)
+  // of bf16 (128-byte swizzle), or 64 bytes of bf16 (bk = 32, 64-byte swizzle)
+  cuuint32_t box[2] = {(cuuint32_t)bk, (cuuint32_t)bn};
   cuuint32_t estr[2] = {1u, 1u};
   CUresult r = fn(map, prec == kPrecBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
                   2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  prec == kPrecBF16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+                  bk * esz == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return set_error(h, ONNXB200_ERR_EXECUTION, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
@@ -172,7 +172,7 @@ void conv_plan_free(onnxb200_conv_plan* p) {
 int conv_plan_init(onnxb200_handle* h, const onnxb200_conv_desc* din, int cs_in, const float* w,
                    const float* bias, const float* bn_scale, const float* bn_bias,
                    const float* bn_mean, const float* bn_var, onnxb200_conv_plan* p, void* scratch,
-                   size_t scratch_bytes, size_t* scratch_used) {
+                   size_t scratch_bytes, size_t* scratch_used, bool a_bf16, bool out_bf16) {
   int rc = resolve_conv_desc(h, din, &p->d, &p->oh, &p->ow);
   if (rc) return rc;
   const onnxb200_conv_desc& d = p->d;
@@ -186,16 +186,20 @@ int conv_plan_init(onnxb200_handle* h, const onnxb200_conv_desc* din, int cs_in,
   p->cs_in = cs_in;
   p->use_tc = d.group == 1 && p->prec != kPrecFP32 && d.c_out % 4 == 0 && cs_in % 4 == 0 &&
               d.kh * d.kw * cs_in < (1 << 30);
+  if ((a_bf16 || out_bf16) && (!p->use_tc || p->prec != kPrecBF16 || (a_bf16 && cs_in % 64)))
+    return set_error(h, ONNXB200_ERR_UNSUPPORTED, "Conv: bf16 storage needs the BF16 tensor-core path");
+  p->a_bf16 = a_bf16;
+  p->out_bf16 = out_bf16;
   const int CO = (int)d.c_out;
   size_t need = 0;
   size_t off_hi = 0, off_lo = 0, off_scale = 0, off_shift = 0, off_w = 0;
-  p->pairs = p->use_tc && cs_in == 4 && d.stride_w == 2 && d.dil_w == 1 &&
+  p->pairs = p->use_tc && !a_bf16 && cs_in == 4 && d.stride_w == 2 && d.dil_w == 1 &&
              d.w % 2 == 0 && d.kw > 1;
   const int kwp = (int)((d.kw + (d.pad_left & 1) + 1) / 2);  // pair taps
   if (p->use_tc) {
     p->K = p->pairs ? (int)(d.kh * kwp * 8) : (int)(d.kh * d.kw * cs_in);
-    p->kpad = igemm_kpad(p->K, p->prec);
-    p->num_kb = p->kpad / igemm_block_k(p->prec);
+    p->kpad = igemm_kpad(p->K, p->prec, a_bf16);
+    p->num_kb = p->kpad / igemm_block_k(p->prec, a_bf16);
     const size_t esz = p->prec == kPrecBF16 ? 2 : 4;
     const size_t wbytes = align_up((size_t)CO * p->kpad * esz);
     off_hi = need;
@@ -250,9 +254,10 @@ int conv_plan_init(onnxb200_handle* h, const onnxb200_conv_desc* din, int cs_in,
     q.Nc = CO;
     q.batches = 1;
     p->bn = igemm_pick_bn(q, p->prec, h->num_sms);
-    rc = encode_weight_map(h, &p->tm_hi, p->w_hi, CO, p->kpad, p->prec, p->bn);
+    const int bk = igemm_block_k(p->prec, a_bf16);
+    rc = encode_weight_map(h, &p->tm_hi, p->w_hi, CO, p->kpad, p->prec, p->bn, bk);
     if (rc) return rc;
-    rc = encode_weight_map(h, &p->tm_lo, p->w_lo ? p->w_lo : p->w_hi, CO, p->kpad, p->prec, p->bn);
+    rc = encode_weight_map(h, &p->tm_lo, p->w_lo ? p->w_lo : p->w_hi, CO, p->kpad, p->prec, p->bn, bk);
     if (rc) return rc;
   } else {
     p->w_oihw = reinterpret_cast<float*>(basep + off_w);
@@ -321,6 +326,8 @@ int conv_plan_exec_nhwc(onnxb200_handle* h, const onnxb200_conv_plan* p, const f
       q.sw = 1;
       q.pw = (int)((d.pad_left + 1) / 2);
     }
+    q.a_bf16 = p->a_bf16;
+    q.out_bf16 = p->out_bf16;
     q.a_mode = pick_a_mode(q, p->prec);
     CUtensorMap am{};
     if (q.a_mode != kALoadGather) {
@@ -344,7 +351,7 @@ int conv_plan_exec_nhwc(onnxb200_handle* h, const onnxb200_conv_plan* p, const f
 int conv_dual_plan_init(onnxb200_handle* h, const onnxb200_conv_desc* d1, int cs1, const float* w1,
                         const ConvBranchBN& bn1, const onnxb200_conv_desc* d2, int cs2, const float* w2,
                         const ConvBranchBN& bn2, onnxb200_conv_plan* p, void* scratch, size_t scratch_bytes,
-                        size_t* scratch_used) {
+                        size_t* scratch_used, bool a_bf16, bool out_bf16) {
   onnxb200_conv_desc r2;
   int64_t oh2 = 0, ow2 = 0;
   int rc = resolve_conv_desc(h, d1, &p->d, &p->oh, &p->ow);
@@ -360,13 +367,18 @@ int conv_dual_plan_init(onnxb200_handle* h, const onnxb200_conv_desc* d1, int cs
   p->cs_in = cs1;
   p->use_tc = true;
   p->pairs = false;
+  if ((a_bf16 || out_bf16) && (p->prec != kPrecBF16 || (a_bf16 && (a.c % 64 || r2.c % 64))))
+    return set_error(h, ONNXB200_ERR_UNSUPPORTED, "Conv: bf16 storage needs the BF16 tensor-core path");
+  const int bk = igemm_block_k(p->prec, a_bf16);
+  p->a_bf16 = a_bf16;
+  p->out_bf16 = out_bf16;
   p->dual = true;
   p->d2 = r2;
   p->cs2 = cs2;
-  p->kb_split = (int)(a.c / 32);
+  p->kb_split = (int)(a.c / bk);
   p->K = (int)(a.c + r2.c);
   p->kpad = p->K;
-  p->num_kb = p->K / 32;
+  p->num_kb = p->K / bk;
   const size_t esz = p->prec == kPrecBF16 ? 2 : 4;
   const size_t wbytes = align_up((size_t)CO * p->kpad * esz);
   size_t need = wbytes * (p->prec == kPrec3xTF32 ? 2 : 1);
@@ -416,9 +428,9 @@ int conv_dual_plan_init(onnxb200_handle* h, const onnxb200_conv_desc* d1, int cs
   q.Nc = CO;
   q.batches = 1;
   p->bn = igemm_pick_bn(q, p->prec, h->num_sms);
-  rc = encode_weight_map(h, &p->tm_hi, p->w_hi, CO, p->kpad, p->prec, p->bn);
+  rc = encode_weight_map(h, &p->tm_hi, p->w_hi, CO, p->kpad, p->prec, p->bn, bk);
   if (rc) return rc;
-  return encode_weight_map(h, &p->tm_lo, p->w_lo ? p->w_lo : p->w_hi, CO, p->kpad, p->prec, p->bn);
+  return encode_weight_map(h, &p->tm_lo, p->w_lo ? p->w_lo : p->w_hi, CO, p->kpad, p->prec, p->bn, bk);
 }
 
 bool dual_conv_supported(const onnxb200_conv_desc& a, int cs1, const onnxb200_conv_desc& b, int cs2) {
@@ -460,6 +472,8 @@ int conv_dual_exec_nhwc(onnxb200_handle* h, const onnxb200_conv_plan* p, const f
   q.m_tiles = (q.M + 127) / 128;
   q.n_tiles = (q.Nc + p->bn - 1) / p->bn;
   q.a_mode = kALoadTma2d;
+  q.a_bf16 = p->a_bf16;
+  q.out_bf16 = p->out_bf16;
   q.kb_split = p->kb_split;
   q.x2 = x2;
   q.H2 = (int)p->d2.h;

@@ -60,13 +60,14 @@ struct GTensor {
   int last_use = -1;           // step index
   int alias_of = -1;           // Flatten view of another tensor
   bool nhwc = false;           // rank-4 image tensor stored NHWC (else row-major as given)
+  bool bf16 = false;           // NHWC activation stored as bf16 (BF16 precision)
   int64_t numel() const {
     int64_t n = 1;
     for (auto v : shape) n *= v;
     return n;
   }
   size_t bytes() const {
-    if (nhwc) return (size_t)shape[0] * shape[2] * shape[3] * (cs ? cs : shape[1]) * 4;
+    if (nhwc) return (size_t)shape[0] * shape[2] * shape[3] * (cs ? cs : shape[1]) * (bf16 ? 2 : 4);
     return (size_t)numel() * 4;
   }
 };
@@ -704,6 +705,7 @@ extern "C" int onnxb200_graph_build(onnxb200_handle* h, const onnxb200_node* nod
     int x, w, b, bn;  // tensor ids / node
     int dual_head, dual_bn;  // second branch (nodes) of a two-source step, or -1
     int head;                // the Conv node
+    int out;                 // the step's output tensor
   };
   std::vector<PendingConv> pconv;
   struct PendingGemm {
@@ -740,7 +742,7 @@ extern "C" int onnxb200_graph_build(onnxb200_handle* h, const onnxb200_node* nod
       if (f.dual_head >= 0) s.in.push_back(nodes[f.dual_head].in[0]);
       s.conv = (int)g->plans.size();
       g->plans.emplace_back();
-      pconv.push_back({s.conv, d, x, nd.in[1], has_b ? nd.in[2] : -1, f.bn, f.dual_head, f.dual_bn, f.head});
+      pconv.push_back({s.conv, d, x, nd.in[1], has_b ? nd.in[2] : -1, f.bn, f.dual_head, f.dual_bn, f.head, f.out});
     } else if (nd.op == "MaxPool") {
       auto k = nd.getv("kernel_shape", {});
       auto st = nd.getv("strides", {1, 1});
@@ -887,6 +889,70 @@ extern "C" int onnxb200_graph_build(onnxb200_handle* h, const onnxb200_node* nod
     g->steps.push_back(s);
   }
 
+  // ---------------------------------------------------------------- bf16 activations
+  // In BF16 precision, the image tensors that convolutions (tensor cores) and
+  // max pools produce are stored as bf16 when every step that reads them can:
+  // a convolution reading them as its input (whole 64-channel taps) or residual,
+  // a max pool (bf16 in and out), a global average pool (fp32 out).  A
+  // convolution's two sources share one storage type, as do its residual and
+  // output, and a bf16 input needs a bf16 output.  Graph inputs and outputs stay
+  // fp32.  Decided by elimination until nothing changes.
+  if (h->opts.precision == kPrecBF16) {
+    std::vector<int> pc_of(g->steps.size(), -1);
+    for (size_t i = 0; i < pconv.size(); ++i)
+      for (size_t si = 0; si < g->steps.size(); ++si)
+        if (g->steps[si].type == kConv && g->steps[si].conv == pconv[i].plan) pc_of[si] = (int)i;
+    auto tc_conv = [&](int si) {
+      const onnxb200_conv_desc& d = pconv[pc_of[si]].d;
+      return d.group == 1 && d.c_out % 4 == 0;
+    };
+    for (const Step& st : g->steps) {
+      if (st.out < 0) continue;
+      GTensor& t = g->tensors[st.out];
+      t.bf16 = t.nhwc && !t.is_input && !t.is_output && t.alias_of < 0 && t.cs == t.shape[1] &&
+               t.shape[1] % 8 == 0 && ((st.type == kConv && tc_conv((int)(&st - &g->steps[0]))) ||
+                                       st.type == kMaxPool);
+    }
+    // a view (Flatten) of a tensor is read as fp32
+    for (const GTensor& t : g->tensors)
+      if (t.alias_of >= 0) {
+        int b = t.alias_of;
+        while (g->tensors[b].alias_of >= 0) b = g->tensors[b].alias_of;
+        g->tensors[b].bf16 = false;
+      }
+    bool changed = true;
+    while (changed) {
+      changed = false;
+      auto off = [&](int id) {
+        if (id >= 0 && g->tensors[id].bf16) {
+          g->tensors[id].bf16 = false;
+          changed = true;
+        }
+      };
+      for (size_t si = 0; si < g->steps.size(); ++si) {
+        const Step& st = g->steps[si];
+        if (st.type == kConv) {
+          const PendingConv& pc = pconv[pc_of[si]];
+          const int a = st.in[0], out = st.out;
+          const bool dual = pc.dual_head >= 0;
+          const int res = (!dual && st.in.size() > 1) ? st.in[1] : -1;
+          const int x2 = dual ? st.in[1] : -1;
+          if (g->tensors[a].bf16 && (g->tensors[a].shape[1] % 64 || !tc_conv((int)si))) off(a);
+          if (x2 >= 0 && g->tensors[x2].bf16 && g->tensors[x2].shape[1] % 64) off(x2);
+          if (x2 >= 0 && g->tensors[a].bf16 != g->tensors[x2].bf16) { off(a); off(x2); }
+          if (res >= 0 && g->tensors[res].bf16 != g->tensors[out].bf16) { off(res); off(out); }
+          if (g->tensors[a].bf16 && !g->tensors[out].bf16) off(a);
+        } else if (st.type == kMaxPool) {
+          if (g->tensors[st.in[0]].bf16 != g->tensors[st.out].bf16) { off(st.in[0]); off(st.out); }
+        } else if (st.type == kGap) {
+          // reads bf16 or fp32
+        } else {
+          for (int t : st.in) off(t);
+        }
+      }
+    }
+  }
+
   // ---------------------------------------------------------------- lifetimes + arena plan
   auto base_of = [&](int t) {
     while (g->tensors[t].alias_of >= 0) t = g->tensors[t].alias_of;
@@ -985,14 +1051,15 @@ extern "C" int onnxb200_graph_build(onnxb200_handle* h, const onnxb200_node* nod
       const onnxb200_conv_desc d2 = conv_desc_of(pc.dual_head);
       return conv_dual_plan_init(h, &pc.d, cs, dptr(pc.w), branch_bn(pc.bn, pc.head), &d2,
                                  x2.cs ? x2.cs : (int)x2.shape[1], dptr(c2.in[1]), branch_bn(pc.dual_bn, pc.dual_head),
-                                 &g->plans[pc.plan], scratch, bytes, used);
+                                 &g->plans[pc.plan], scratch, bytes, used, xt.bf16, g->tensors[pc.out].bf16);
     }
     const float *qb = pc.b >= 0 ? dptr(pc.b) : nullptr, *q1 = nullptr, *q2 = nullptr, *q3 = nullptr, *q4 = nullptr;
     if (pc.bn >= 0) {
       const Node& bn = nodes[pc.bn];
       q1 = dptr(bn.in[1]); q2 = dptr(bn.in[2]); q3 = dptr(bn.in[3]); q4 = dptr(bn.in[4]);
     }
-    return conv_plan_init(h, &pc.d, cs, dptr(pc.w), qb, q1, q2, q3, q4, &g->plans[pc.plan], scratch, bytes, used);
+    return conv_plan_init(h, &pc.d, cs, dptr(pc.w), qb, q1, q2, q3, q4, &g->plans[pc.plan], scratch, bytes, used,
+                          xt.bf16, g->tensors[pc.out].bf16);
   };
   std::vector<size_t> plan_off(pconv.size());
   size_t wtotal = 0;
@@ -1167,16 +1234,25 @@ static int run_steps(onnxb200_graph* g, const float* const* uin, float* const* u
       case kMaxPool: {
         const GTensor& x = g->tensors[s.in[0]];
         const GTensor& y = g->tensors[s.out];
-        rc = maxpool_nhwc_launch(T(s.in[0]), (int)x.shape[0], (int)x.shape[1], x.cs, (int)x.shape[2],
-                                 (int)x.shape[3], s.kh, s.kw, s.sh, s.sw, s.pt, s.pl, (int)y.shape[2],
-                                 (int)y.shape[3], T(s.out), nullptr, st);
+        if (x.bf16)
+          rc = maxpool_nhwc_bf16_launch(T(s.in[0]), (int)x.shape[0], (int)x.shape[1], (int)x.shape[2],
+                                        (int)x.shape[3], s.kh, s.kw, s.sh, s.sw, s.pt, s.pl, (int)y.shape[2],
+                                        (int)y.shape[3], T(s.out), st);
+        else
+          rc = maxpool_nhwc_launch(T(s.in[0]), (int)x.shape[0], (int)x.shape[1], x.cs, (int)x.shape[2],
+                                   (int)x.shape[3], s.kh, s.kw, s.sh, s.sw, s.pt, s.pl, (int)y.shape[2],
+                                   (int)y.shape[3], T(s.out), nullptr, st);
         h->launches++;
         break;
       }
       case kGap: {
         const GTensor& x = g->tensors[s.in[0]];
-        rc = gap_nhwc_launch(T(s.in[0]), (int)x.shape[0], (int)x.shape[1], (int)(x.shape[2] * x.shape[3]),
-                             T(s.out), st);
+        if (x.bf16)
+          rc = gap_nhwc_bf16_launch(T(s.in[0]), (int)x.shape[0], (int)x.shape[1],
+                                    (int)(x.shape[2] * x.shape[3]), T(s.out), st);
+        else
+          rc = gap_nhwc_launch(T(s.in[0]), (int)x.shape[0], (int)x.shape[1], (int)(x.shape[2] * x.shape[3]),
+                               T(s.out), st);
         h->launches++;
         break;
       }
@@ -1270,7 +1346,7 @@ static int run_steps(onnxb200_graph* g, const float* const* uin, float* const* u
 static void step_work(const onnxb200_graph* g, const Step& s, int* kind, double* flops, double* bytes) {
   auto tb = [&](int id) -> double {
     const GTensor& t = g->tensors[id];
-    return (double)t.numel() * 4.0;
+    return (double)t.numel() * (t.bf16 ? 2.0 : 4.0);
   };
   *flops = 0;
   *bytes = 0;
@@ -1543,5 +1619,7 @@ extern "C" int onnxb200_graph_get_stats(const onnxb200_graph* g, onnxb200_graph_
   s->arena_bytes = (int64_t)g->arena_bytes;
   s->weight_bytes = (int64_t)g->weight_bytes;
   s->captured = g->cge != nullptr;
+  s->bf16_tensors = 0;
+  for (const GTensor& t : g->tensors) s->bf16_tensors += t.bf16 ? 1 : 0;
   return ONNXB200_OK;
 }

@@ -66,9 +66,13 @@ int igemm_launch(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap&
     return (int)cudaErrorMisalignedAddress;
   // two sources: source 1 a [pixels][Cs] matrix of whole k-blocks, source 2 a
   // 1x1 convolution of whole k-blocks at the same output pixels
+  const int bk = igemm_block_k(precision, p.a_bf16 != 0);
+  // bf16 activations: whole taps per k-block through TMA, no padding
+  if (p.a_bf16 && (p.a_mode == kALoadGather || p.a_mode == kALoadIm2colTaps || p.Cs % bk || p.K % bk))
+    return (int)cudaErrorInvalidValue;
   if (p.kb_split &&
-      (p.a_mode != kALoadTma2d || p.Cs != p.kb_split * 32 || p.batches != 1 || p.a_off || !p.x2 ||
-       mis(p.x2) || p.Cs2 % 32 || p.s2 < 1 || p.num_kb != p.kb_split + p.Cs2 / 32 ||
+      (p.a_mode != kALoadTma2d || p.Cs != p.kb_split * bk || p.batches != 1 || p.a_off || !p.x2 ||
+       mis(p.x2) || p.Cs2 % bk || p.s2 < 1 || p.num_kb != p.kb_split + p.Cs2 / bk ||
        (p.a_mode2 != kALoadTma2d && p.a_mode2 != kALoadIm2col) ||
        (p.a_mode2 == kALoadTma2d && (p.s2 != 1 || p.H2 != p.OH || p.W2 != p.OW))))
     return (int)cudaErrorInvalidValue;
@@ -79,8 +83,14 @@ int igemm_launch(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap&
 
 int pick_a_mode(const IgemmParams& p, int precision) {
   // A k-block is 32 fp32 (one 128-byte TMA row per pixel): 32 channels of one
-  // filter tap, or 32 / Cs whole taps of a 4-, 8- or 16-channel tensor
+  // filter tap, or 32 / Cs whole taps of a 4-, 8- or 16-channel tensor.  With
+  // bf16 activations it is 64 channels of one tap, TMA only (Cs % 64 == 0).
   const bool single_tap = p.K == p.Cs;
+  if (p.a_bf16) {
+    if (p.Cs % 64) return kALoadGather;  // refused by igemm_launch
+    if (single_tap && p.sh == 1 && p.sw == 1 && p.ph == 0 && p.pw == 0 && p.OH == p.Hin && p.OW == p.Win)
+      return kALoadTma2d;
+  }
   if (single_tap && p.sh == 1 && p.sw == 1 && p.ph == 0 && p.pw == 0 && p.OH == p.Hin &&
       p.OW == p.Win)  // rows of A are rows of the [pixels][channels] matrix; the
                       // box of the last k-block may run past Cs (zero fill)
@@ -122,15 +132,18 @@ void* driver_fn(const char* name) {
 
 int encode_a_map(const IgemmParams& p, int n, CUtensorMap* map) {
   void* base = const_cast<float*>(p.x);
+  const int esz_a = p.a_bf16 ? 2 : 4;
   if (p.a_mode == kALoadTma2d) {
     static EncodeTiledFn2 fn = reinterpret_cast<EncodeTiledFn2>(driver_fn("cuTensorMapEncodeTiled"));
     if (!fn) return (int)CUDA_ERROR_NOT_FOUND;
     // n = number of rows of the [rows][Cs] matrix (pixels of the batch, or all A rows)
+    const int esz = p.a_bf16 ? 2 : 4;
     cuuint64_t dims[2] = {(cuuint64_t)p.Cs, (cuuint64_t)n};
-    cuuint64_t strides[1] = {(cuuint64_t)p.Cs * 4};
-    cuuint32_t box[2] = {32u, (cuuint32_t)kBM};
+    cuuint64_t strides[1] = {(cuuint64_t)p.Cs * esz};
+    cuuint32_t box[2] = {p.a_bf16 ? 64u : 32u, (cuuint32_t)kBM};
     cuuint32_t es[2] = {1u, 1u};
-    return (int)fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, es,
+    return (int)fn(map, p.a_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base,
+                   dims, strides, box, es,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   }
@@ -138,8 +151,8 @@ int encode_a_map(const IgemmParams& p, int n, CUtensorMap* map) {
   if (!fn) return (int)CUDA_ERROR_NOT_FOUND;
   // NHWC tensor, dims innermost first: C, W, H, N (n = images)
   cuuint64_t dims[4] = {(cuuint64_t)p.Cs, (cuuint64_t)p.Win, (cuuint64_t)p.Hin, (cuuint64_t)n};
-  cuuint64_t strides[3] = {(cuuint64_t)p.Cs * 4, (cuuint64_t)p.Win * p.Cs * 4,
-                           (cuuint64_t)p.Hin * p.Win * p.Cs * 4};
+  cuuint64_t strides[3] = {(cuuint64_t)p.Cs * esz_a, (cuuint64_t)p.Win * p.Cs * esz_a,
+                           (cuuint64_t)p.Hin * p.Win * p.Cs * esz_a};
   // Bounding box of the base (top-left) input pixel of every output pixel:
   // W from -pw to (OW-1)*sw - pw, H likewise; traversal stride = conv stride.
   int lower[2] = {-p.pw, -p.ph};
@@ -148,8 +161,9 @@ int encode_a_map(const IgemmParams& p, int n, CUtensorMap* map) {
   // taps mode: one box = all Cs channels (16 to 64 bytes) of 128 pixels for one
   // tap, unswizzled; otherwise 32 channels in 128-byte swizzled rows
   const bool taps = p.a_mode == kALoadIm2colTaps;
-  return (int)fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, dims, strides, lower, upper,
-                 taps ? (cuuint32_t)p.Cs : 32u, (cuuint32_t)kBM, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+  return (int)fn(map, p.a_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base,
+                 dims, strides, lower, upper, taps ? (cuuint32_t)p.Cs : (p.a_bf16 ? 64u : 32u),
+                 (cuuint32_t)kBM, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
                  taps ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B,
                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }

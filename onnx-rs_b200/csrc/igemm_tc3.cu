@@ -67,13 +67,21 @@ constexpr int kSmemBudget = 224 * 1024;
 // EG = 16 halves the staging memory so that 3xTF32 with BN = 128 fits four 48 KB
 // operand stages, which pays when the tile's K loop is long.
 
-template <int PREC, int BN, int EG, int NB>
+// AIO (BF16 only): bit 0 = the activations A are stored as bf16 (read by the
+// MMAs straight from shared memory, 64-element k-blocks of 128-byte rows);
+// bit 1 = the output and residual are stored as bf16.
+template <int PREC, int BN, int EG, int NB, int AIO = 0>
 struct Layout {
-  static constexpr int kEpiTile = kBM * EG * 4;
+  static constexpr bool kABf16 = (AIO & 1) != 0;
+  static constexpr bool kOBf16 = (AIO & 2) != 0;
+  static constexpr int kBK = kABf16 ? 64 : 32;  // K elements per k-block (128-byte A rows)
+  static constexpr int kOes = kOBf16 ? 2 : 4;   // bytes per output element
+  static constexpr int kEpiTile = kBM * EG * kOes;
+  static constexpr int kEpiRow = EG * kOes;     // bytes per staging row (64 or 128)
   static constexpr bool kSplit = (PREC == kPrec3xTF32);
   static constexpr bool kBf16 = (PREC == kPrecBF16);
-  static constexpr bool kTmemA = kSplit || kBf16;  // converters write A to TMEM
-  static constexpr int kARaw = kBM * kBK * 4;   // 16 KB
+  static constexpr bool kTmemA = kSplit || (kBf16 && !kABf16);  // converters write A to TMEM
+  static constexpr int kARaw = kBM * kBK * (kABf16 ? 2 : 4);   // 16 KB
   static constexpr int kBBytes = BN * kBK * (kBf16 ? 2 : 4);  // one B operand (hi or lo)
   static constexpr int kStage = kARaw + (kSplit ? 2 : 1) * kBBytes;
   static constexpr int kEpiBytes = 2 * NB * kEpiTile;  // out[NB] + res[NB]
@@ -135,10 +143,26 @@ __device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t saddr) {
 }
 // 128-byte-swizzle layout of a [rows][32 fp32] tile.
 __device__ __forceinline__ uint32_t swz128(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
-// Staging tile of the epilogue: rows of EG fp32, swizzled like its TMA box.
-template <int EG>
+// Staging tile of the epilogue: rows of RB bytes (64 or 128), 16-byte chunk c,
+// swizzled like its TMA box.
+template <int RB>
 __device__ __forceinline__ uint32_t swz_eg(int r, int c) {
-  return EG == 32 ? swz128(r, c) : swz64(r, c);
+  return RB == 128 ? swz128(r, c) : swz64(r, c);
+}
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 h2 = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h2);
+}
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+__device__ __forceinline__ void sts_u4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+__device__ __forceinline__ uint4 lds_u4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr)
+               : "memory");
+  return v;
 }
 __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[16]) { tmem_ld_32x32b_x16(taddr, r); }
 __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[32]) { tmem_ld_32x32b_x32(taddr, r); }
@@ -148,13 +172,14 @@ __device__ __forceinline__ void sts_v4(uint32_t addr, float a, float b, float c,
                : "memory");
 }
 
-template <int PREC, int BN, int EG, int NB>
+template <int PREC, int BN, int EG, int NB, int AIO>
 __global__ void __launch_bounds__(kThreads, 1)
     igemm_tc3_kernel(const __grid_constant__ IgemmParams p, const __grid_constant__ CUtensorMap tm_hi,
                      const __grid_constant__ CUtensorMap tm_lo, const __grid_constant__ CUtensorMap tm_a,
                      const __grid_constant__ CUtensorMap tm_a2, const __grid_constant__ CUtensorMap tm_y,
                      const __grid_constant__ CUtensorMap tm_res) {
-  using L = Layout<PREC, BN, EG, NB>;
+  using L = Layout<PREC, BN, EG, NB, AIO>;
+  constexpr int kBK = L::kBK;
   constexpr int kEG = EG;
   constexpr int kEpiTile = L::kEpiTile;
   constexpr int S1 = L::kS1;
@@ -403,6 +428,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int s = item % S1;
       const int a = item % S2;
       bool ok = mbar_wait(s1_full(s), (item / S1) & 1, abort_flag, p.status);
+      if constexpr (L::kABf16) {
+        // bf16 activations: the MMAs read the stage as it landed (whole taps of
+        // 64-channel multiples, no K padding), so there is nothing to convert
+        if (!ok) break;
+        mbar_arrive(t_full(a));
+        continue;
+      }
       const uint32_t rbase = a_raw + s * L::kARaw;
       // k beyond K: padding of the last k-block (zero weights); never multiply
       // whatever the stage held there
@@ -438,7 +470,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < kBK / 4; ++c)
           st_shared_f4(rbase + swz128(row, c), v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
       }
-      if constexpr (L::kBf16) {
+      if constexpr (L::kBf16 && !L::kABf16) {
         // bf16 pairs (lower k in the low half) into TMEM slot a, once the MMAs of
         // the slot's previous use have completed (see the 3xTF32 case below)
         if (item >= S2) {
@@ -508,11 +540,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t ahi = tmem_base + L::kACol0 + a * L::kAStageCols;  // 3xTF32: A hi | lo
         const uint32_t alo = ahi + kBK;
         const uint64_t da = smem_desc_sw128(a_raw + s * L::kARaw);  // TF32: A as landed
-        const uint64_t dbh = L::kBf16 ? smem_desc_sw64(b_hi + s * L::kBStride)
-                                       : smem_desc_sw128(b_hi + s * L::kBStride);
+        const uint64_t dbh = (L::kBf16 && !L::kABf16) ? smem_desc_sw64(b_hi + s * L::kBStride)
+                                                       : smem_desc_sw128(b_hi + s * L::kBStride);
         uint64_t dbl = 0;
         if constexpr (L::kSplit) dbl = smem_desc_sw128(b_lo + s * L::kBStride);
-        if constexpr (L::kBf16) {
+        if constexpr (L::kABf16) {
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)  // A and B from shared memory, 128-byte rows
+            tc_mma<1>(d_tmem, da + (uint64_t)(kk * 2), dbh + (uint64_t)(kk * 2), idesc_bf, (kin | kk) ? 1u : 0u);
+        } else if constexpr (L::kBf16) {
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk)  // K = 16 bf16 (32 bytes) per MMA
             tc_mma_f16_ts(d_tmem, ahi + kk * 8, dbh + (uint64_t)(kk * 2), idesc_bf, (kin | kk) ? 1u : 0u);
@@ -700,10 +736,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (p.res && rows_in) {
             w = mbar_wait(res_full(warp, buf), (grp / NB) & 1, abort_flag, p.status);
             if (w && lane == 0) res_out &= ~(1u << buf);
+            if constexpr (L::kOBf16) {
 #pragma unroll
-            for (int q4 = 0; q4 < kEG / 4; ++q4) {
-              const float4 rv = ld_shared_f4(res_st + buf * kEpiTile + swz_eg<kEG>(et, q4));
-              v[4 * q4] += rv.x; v[4 * q4 + 1] += rv.y; v[4 * q4 + 2] += rv.z; v[4 * q4 + 3] += rv.w;
+              for (int q8 = 0; q8 < kEG / 8; ++q8) {
+                const uint4 rv = lds_u4(res_st + buf * kEpiTile + swz_eg<L::kEpiRow>(et, q8));
+                v[8 * q8] += bf16_lo(rv.x); v[8 * q8 + 1] += bf16_hi(rv.x);
+                v[8 * q8 + 2] += bf16_lo(rv.y); v[8 * q8 + 3] += bf16_hi(rv.y);
+                v[8 * q8 + 4] += bf16_lo(rv.z); v[8 * q8 + 5] += bf16_hi(rv.z);
+                v[8 * q8 + 6] += bf16_lo(rv.w); v[8 * q8 + 7] += bf16_hi(rv.w);
+              }
+            } else {
+#pragma unroll
+              for (int q4 = 0; q4 < kEG / 4; ++q4) {
+                const float4 rv = ld_shared_f4(res_st + buf * kEpiTile + swz_eg<L::kEpiRow>(et, q4));
+                v[4 * q4] += rv.x; v[4 * q4 + 1] += rv.y; v[4 * q4 + 2] += rv.z; v[4 * q4 + 3] += rv.w;
+              }
             }
           }
           if (p.relu) {
@@ -718,9 +765,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           const uint32_t ost = out_st + buf * kEpiTile;
+          if constexpr (L::kOBf16) {
 #pragma unroll
-          for (int q4 = 0; q4 < kEG / 4; ++q4)
-            sts_v4(ost + swz_eg<kEG>(et, q4), v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
+            for (int q8 = 0; q8 < kEG / 8; ++q8)
+              sts_u4(ost + swz_eg<L::kEpiRow>(et, q8), pack_bf16x2(v[8 * q8], v[8 * q8 + 1]),
+                     pack_bf16x2(v[8 * q8 + 2], v[8 * q8 + 3]), pack_bf16x2(v[8 * q8 + 4], v[8 * q8 + 5]),
+                     pack_bf16x2(v[8 * q8 + 6], v[8 * q8 + 7]));
+          } else {
+#pragma unroll
+            for (int q4 = 0; q4 < kEG / 4; ++q4)
+              sts_v4(ost + swz_eg<L::kEpiRow>(et, q4), v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
+          }
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0 && rows_in) {
@@ -772,40 +827,40 @@ EncodeTiledFn3 tiled_fn() {
   return fn;
 }
 
-// [batches][rows][cols] fp32 output / residual with row stride ld, batch stride
-// bstride (elements); 32-row x eg boxes (one per epilogue warp; eg = 16 or 32
-// columns, 64- or 128-byte swizzle).
-int encode_out_map(const float* base, int cols, int rows, int batches, int ld, long long bstride,
-                   int eg, CUtensorMap* map) {
+// [batches][rows][cols] output / residual (fp32, or bf16 when es == 2) with
+// row stride ld, batch stride bstride (elements); 32-row x eg boxes (one per
+// epilogue warp), 64- or 128-byte rows with the matching swizzle.
+int encode_out_map(const void* base, int cols, int rows, int batches, int ld, long long bstride,
+                   int eg, int es_bytes, CUtensorMap* map) {
   EncodeTiledFn3 fn = tiled_fn();
   if (!fn) return (int)CUDA_ERROR_NOT_FOUND;
   const long long bs = batches > 1 ? bstride : (long long)rows * ld;
   cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)batches};
-  cuuint64_t strides[2] = {(cuuint64_t)ld * 4, (cuuint64_t)bs * 4};
+  cuuint64_t strides[2] = {(cuuint64_t)ld * es_bytes, (cuuint64_t)bs * es_bytes};
   cuuint32_t box[3] = {(cuuint32_t)eg, 32u, 1u};
   cuuint32_t es[3] = {1u, 1u, 1u};
-  return (int)fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box,
-                 es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                 eg == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+  return (int)fn(map, es_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3,
+                 const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                 eg * es_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
 
-template <int PREC, int BN, int EG, int NB>
+template <int PREC, int BN, int EG, int NB, int AIO = 0>
 int launch3_t(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap& lo,
               const CUtensorMap& am, const CUtensorMap& am2, int num_sms, cudaStream_t st) {
-  using L = Layout<PREC, BN, EG, NB>;
+  using L = Layout<PREC, BN, EG, NB, AIO>;
   static bool attr_set = false;
   if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(igemm_tc3_kernel<PREC, BN, EG, NB>,
+    cudaError_t e = cudaFuncSetAttribute(igemm_tc3_kernel<PREC, BN, EG, NB, AIO>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
     if (e != cudaSuccess) return (int)e;
     attr_set = true;
   }
   CUtensorMap ym{}, rm{};
-  int er = encode_out_map(p.y, p.Nc, p.M, p.batches, p.ldy, p.y_bstride, EG, &ym);
+  int er = encode_out_map(p.y, p.Nc, p.M, p.batches, p.ldy, p.y_bstride, EG, L::kOes, &ym);
   if (er) return (int)cudaErrorInvalidValue;
   if (p.res) {
-    er = encode_out_map(p.res, p.Nc, p.M, p.batches, p.ldr, p.y_bstride, EG, &rm);
+    er = encode_out_map(p.res, p.Nc, p.M, p.batches, p.ldr, p.y_bstride, EG, L::kOes, &rm);
     if (er) return (int)cudaErrorInvalidValue;
   }
   const int total = p.m_tiles * p.n_tiles * p.batches;
@@ -823,7 +878,7 @@ int launch3_t(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap& lo
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return (int)cudaLaunchKernelEx(&cfg, igemm_tc3_kernel<PREC, BN, EG, NB>, p, hi, lo, am, am2, ym, rm);
+  return (int)cudaLaunchKernelEx(&cfg, igemm_tc3_kernel<PREC, BN, EG, NB, AIO>, p, hi, lo, am, am2, ym, rm);
 }
 
 }  // namespace
@@ -854,6 +909,22 @@ int igemm3_launch(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap
     return short_k ? launch3_t<kPrecTF32, 128, 32, 4>(p, hi, lo, am, am2, num_sms, st)
                    : launch3_t<kPrecTF32, 128, 32, 2>(p, hi, lo, am, am2, num_sms, st);
   if (precision == kPrecTF32 && bn == 256) return launch3_t<kPrecTF32, 256, 32, 2>(p, hi, lo, am, am2, num_sms, st);
+  // bf16 activations (AIO bit 0) and / or bf16 outputs (bit 1)
+  const int aio = (p.a_bf16 ? 1 : 0) | (p.out_bf16 ? 2 : 0);
+  if (aio && precision != kPrecBF16) return (int)cudaErrorInvalidValue;
+  if (aio == 3 && bn == 64)
+    return short_k ? launch3_t<kPrecBF16, 64, 32, 4, 3>(p, hi, lo, am, am2, num_sms, st)
+                   : launch3_t<kPrecBF16, 64, 32, 2, 3>(p, hi, lo, am, am2, num_sms, st);
+  if (aio == 3 && bn == 128)
+    return short_k ? launch3_t<kPrecBF16, 128, 32, 4, 3>(p, hi, lo, am, am2, num_sms, st)
+                   : launch3_t<kPrecBF16, 128, 32, 2, 3>(p, hi, lo, am, am2, num_sms, st);
+  if (aio == 2 && bn == 64)
+    return short_k ? launch3_t<kPrecBF16, 64, 32, 4, 2>(p, hi, lo, am, am2, num_sms, st)
+                   : launch3_t<kPrecBF16, 64, 32, 2, 2>(p, hi, lo, am, am2, num_sms, st);
+  if (aio == 2 && bn == 128)
+    return short_k ? launch3_t<kPrecBF16, 128, 32, 4, 2>(p, hi, lo, am, am2, num_sms, st)
+                   : launch3_t<kPrecBF16, 128, 32, 2, 2>(p, hi, lo, am, am2, num_sms, st);
+  if (aio) return (int)cudaErrorInvalidValue;
   if (precision == kPrecBF16 && bn == 64)
     return short_k ? launch3_t<kPrecBF16, 64, 32, 4>(p, hi, lo, am, am2, num_sms, st)
                    : launch3_t<kPrecBF16, 64, 32, 2>(p, hi, lo, am, am2, num_sms, st);

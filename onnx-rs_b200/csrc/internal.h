@@ -45,6 +45,10 @@ struct onnxb200_conv_plan {
   // input is read as [N][H][W/2][8] and the convolution runs with stride 1 over
   // ceil((KW + pw%2)/2) pair taps -- the same memory, half the TMA box rows.
   bool pairs = false;
+  // BF16 precision in a graph: the input activations (x, x2) are stored as bf16
+  // (64-element k-blocks), and / or the output and residual are.
+  bool a_bf16 = false;
+  bool out_bf16 = false;
   // Two sources (conv_dual_plan_init): a 1x1 stride-1 convolution of x (this
   // descriptor) plus a 1x1 convolution of x2 (d2, stride d2.stride_h) at the
   // same output pixels, weights packed side by side along K with each branch's
@@ -63,7 +67,7 @@ int ensure_workspace(onnxb200_handle* h, size_t bytes);
 
 // Encodes a 2-D TMA map over a [rows][kpad] K-major weight matrix.
 int encode_weight_map(onnxb200_handle* h, CUtensorMap* map, const void* base, int rows, int kpad,
-                      int prec, int bn);
+                      int prec, int bn, int bk = 32);
 
 // Resolves auto_pad / defaults and validates a conv descriptor.
 int resolve_conv_desc(onnxb200_handle* h, const onnxb200_conv_desc* in, onnxb200_conv_desc* out,
@@ -76,7 +80,8 @@ int resolve_conv_desc(onnxb200_handle* h, const onnxb200_conv_desc* in, onnxb200
 int conv_plan_init(onnxb200_handle* h, const onnxb200_conv_desc* d, int cs_in, const float* w,
                    const float* bias, const float* bn_scale, const float* bn_bias,
                    const float* bn_mean, const float* bn_var, onnxb200_conv_plan* p,
-                   void* scratch, size_t scratch_bytes, size_t* scratch_used);
+                   void* scratch, size_t scratch_bytes, size_t* scratch_used, bool a_bf16 = false,
+                   bool out_bf16 = false);
 void conv_plan_free(onnxb200_conv_plan* p);
 
 // BatchNormalization of one branch of a two-source convolution (all device
@@ -97,7 +102,7 @@ bool dual_conv_supported(const onnxb200_conv_desc& d1, int cs1, const onnxb200_c
 int conv_dual_plan_init(onnxb200_handle* h, const onnxb200_conv_desc* d1, int cs1, const float* w1,
                         const ConvBranchBN& bn1, const onnxb200_conv_desc* d2, int cs2, const float* w2,
                         const ConvBranchBN& bn2, onnxb200_conv_plan* p, void* scratch, size_t scratch_bytes,
-                        size_t* scratch_used);
+                        size_t* scratch_used, bool a_bf16 = false, bool out_bf16 = false);
 int conv_dual_exec_nhwc(onnxb200_handle* h, const onnxb200_conv_plan* p, const float* x1, const float* x2,
                         float* y);
 

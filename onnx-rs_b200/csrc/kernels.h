@@ -54,6 +54,11 @@ struct IgemmParams {
   const float* x2;
   int H2, W2, Cs2, s2;
   int a_mode2;             // kALoadTma2d (stride 1) or kALoadIm2col
+  // BF16 precision only: the activations (x, x2) are stored as bf16 (k-blocks of
+  // 64 elements, Cs a multiple of 64, TMA modes only), and / or the output y and
+  // the residual are stored as bf16.  x / y / res then point at bf16 data.
+  int a_bf16;
+  int out_bf16;
 };
 
 enum ALoadMode { kALoadGather = 0, kALoadTma2d = 1, kALoadIm2col = 2, kALoadIm2colTaps = 3 };
@@ -86,11 +91,12 @@ int igemm3_launch(const IgemmParams& p, const CUtensorMap& tm_hi, const CUtensor
                   const CUtensorMap& tm_a, const CUtensorMap& tm_a2, int precision, int bn, int num_sms,
                   cudaStream_t stream);
 
-// K elements per k-block of the kernel used for a precision (p.num_kb = Kpad / this).
-inline int igemm_block_k(int) { return 32; }
+// K elements per k-block of the kernel used for a precision (p.num_kb = Kpad / this):
+// 32, or 64 when the activations are stored as bf16 (128-byte rows either way).
+inline int igemm_block_k(int, bool a_bf16 = false) { return a_bf16 ? 64 : 32; }
 // Padded K (row length of the packed weights): a whole number of k-blocks.
-inline int igemm_kpad(long long K, int precision) {
-  const int bk = igemm_block_k(precision);
+inline int igemm_kpad(long long K, int precision, bool a_bf16 = false) {
+  const int bk = igemm_block_k(precision, a_bf16);
   return (int)((K + bk - 1) / bk * bk);
 }
 
@@ -143,6 +149,12 @@ int nhwc_to_nchw_launch(const float* x, int N, int C, int H, int W, int Cs, floa
 int maxpool_nhwc_launch(const float* x, int N, int C, int Cs, int H, int W, int KH, int KW,
                         int sh, int sw, int pt, int pl, int OH, int OW, float* y,
                         long long* indices, cudaStream_t stream);
+
+// MaxPool over bf16 NHWC (channels packed, C % 8 == 0), bf16 out.
+int maxpool_nhwc_bf16_launch(const void* x, int N, int C, int H, int W, int KH, int KW, int sh, int sw,
+                             int pt, int pl, int OH, int OW, void* y, cudaStream_t stream);
+// Global average pool of bf16 NHWC (C % 8 == 0) into fp32 y[n][c].
+int gap_nhwc_bf16_launch(const void* x, int N, int C, int HW, float* y, cudaStream_t stream);
 
 // Global average pool over NHWC: y[n][c] = mean over H*W.
 int gap_nhwc_launch(const float* x, int N, int C, int HW, float* y, cudaStream_t stream);

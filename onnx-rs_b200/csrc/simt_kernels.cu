@@ -566,6 +566,91 @@ __global__ void gap_nhwc_scalar_kernel(const float* __restrict__ x, int C, int H
   y[(long long)n * C + c] = s / (float)HW;
 }
 
+// bf16 activations (BF16 precision in a graph): 8 channels (16 bytes) per
+// thread, compared / summed in fp32.
+__device__ __forceinline__ void bf16x8_to_f32(const uint4 v, float (&f)[8]) {
+  f[0] = __uint_as_float(v.x << 16); f[1] = __uint_as_float(v.x & 0xFFFF0000u);
+  f[2] = __uint_as_float(v.y << 16); f[3] = __uint_as_float(v.y & 0xFFFF0000u);
+  f[4] = __uint_as_float(v.z << 16); f[5] = __uint_as_float(v.z & 0xFFFF0000u);
+  f[6] = __uint_as_float(v.w << 16); f[7] = __uint_as_float(v.w & 0xFFFF0000u);
+}
+
+__global__ void maxpool_nhwc_bf16_kernel(const uint4* __restrict__ x, int N, int C8, int H, int W, int KH,
+                                         int KW, int sh, int sw, int pt, int pl, int OH, int OW,
+                                         uint4* __restrict__ y) {
+  const long long total = (long long)N * OH * OW * C8;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int c8 = (int)(i % C8);
+    const long long pix = i / C8;
+    const int ow = (int)(pix % OW);
+    const int oh = (int)((pix / OW) % OH);
+    const int n = (int)(pix / ((long long)OW * OH));
+    float m[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) m[e] = -3.40282347e+38f;
+    for (int r = 0; r < KH; ++r) {
+      const int ih = oh * sh - pt + r;
+      if ((unsigned)ih >= (unsigned)H) continue;
+      for (int q = 0; q < KW; ++q) {
+        const int iw = ow * sw - pl + q;
+        if ((unsigned)iw >= (unsigned)W) continue;
+        float f[8];
+        bf16x8_to_f32(x[(((long long)n * H + ih) * W + iw) * C8 + c8], f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) m[e] = fmaxf(m[e], f[e]);
+      }
+    }
+    // the maxima are input values, so the conversion back is exact
+    uint4 o;
+    o.x = (__float_as_uint(m[1]) & 0xFFFF0000u) | (__float_as_uint(m[0]) >> 16);
+    o.y = (__float_as_uint(m[3]) & 0xFFFF0000u) | (__float_as_uint(m[2]) >> 16);
+    o.z = (__float_as_uint(m[5]) & 0xFFFF0000u) | (__float_as_uint(m[4]) >> 16);
+    o.w = (__float_as_uint(m[7]) & 0xFFFF0000u) | (__float_as_uint(m[6]) >> 16);
+    y[pix * C8 + c8] = o;
+  }
+}
+
+int maxpool_nhwc_bf16_launch(const void* x, int N, int C, int H, int W, int KH, int KW, int sh, int sw,
+                             int pt, int pl, int OH, int OW, void* y, cudaStream_t st) {
+  if (C % 8 || ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15))
+    return (int)cudaErrorMisalignedAddress;
+  const long long total = (long long)N * OH * OW * (C / 8);
+  if (total == 0) return 0;
+  maxpool_nhwc_bf16_kernel<<<grid_for(total, kBlock), kBlock, 0, st>>>(
+      static_cast<const uint4*>(x), N, C / 8, H, W, KH, KW, sh, sw, pt, pl, OH, OW, static_cast<uint4*>(y));
+  return (int)cudaGetLastError();
+}
+
+__global__ void gap_nhwc_bf16_kernel(const uint4* __restrict__ x, int C8, int HW, float* __restrict__ y) {
+  const int n = blockIdx.y;
+  const int c8 = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c8 >= C8) return;
+  const uint4* p = x + (long long)n * HW * C8 + c8;
+  float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int i = 0; i < HW; ++i) {
+    float f[8];
+    bf16x8_to_f32(p[(long long)i * C8], f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) s[e] += f[e];
+  }
+  const float cnt = (float)HW;
+  float4* o = reinterpret_cast<float4*>(y + (long long)n * C8 * 8 + 8 * c8);
+  o[0] = make_float4(s[0] / cnt, s[1] / cnt, s[2] / cnt, s[3] / cnt);
+  o[1] = make_float4(s[4] / cnt, s[5] / cnt, s[6] / cnt, s[7] / cnt);
+}
+
+int gap_nhwc_bf16_launch(const void* x, int N, int C, int HW, float* y, cudaStream_t st) {
+  if (N == 0 || C == 0) return 0;
+  if (C % 8 || ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15))
+    return (int)cudaErrorMisalignedAddress;
+  const int c8 = C / 8;
+  const int block = c8 < 128 ? 32 * ((c8 + 31) / 32) : 128;
+  dim3 grid((c8 + block - 1) / block, N);
+  gap_nhwc_bf16_kernel<<<grid, block, 0, st>>>(static_cast<const uint4*>(x), c8, HW, y);
+  return (int)cudaGetLastError();
+}
+
 int gap_nhwc_launch(const float* x, int N, int C, int HW, float* y, cudaStream_t st) {
   if (N == 0 || C == 0) return 0;
   const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15) == 0;

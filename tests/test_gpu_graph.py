@@ -202,6 +202,8 @@ def test_resnet50_fast_modes(ob, oracle, r50_b256, r50_b256_ref64, precision):
     nodes, inits, ins, outs, x = r50_b256
     h = ob.Handle(0, precision=precision)
     g = ob.Graph(h, nodes, inits, ins, outs)
+    if precision == "bf16":  # activations between the convolutions are stored as bf16
+        assert g.stats()["bf16_tensors"] >= 40, g.stats()
     y = g.run([torch.from_numpy(x).cuda()])[0]
     h.synchronize()
     check_logits_fast(y.cpu().numpy(), r50_b256_ref64, f"resnet50 b256/{precision}")
