@@ -259,6 +259,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int my_tiles =
       (blockIdx.x < total_tiles) ? (total_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
   const int total_items = my_tiles * p.num_kb;
+  // The MMAs read A straight from the stage that TMA landed (TF32, bf16
+  // activations) and no stage needs rewriting (no taps-mode boxes, no K
+  // padding): the MMA thread waits for the stage itself and the converter warps
+  // have no work.
+  const bool direct = !L::kTmemA && (p.a_mode == kALoadTma2d || p.a_mode == kALoadIm2col) && p.K % kBK == 0;
 
   if (warp >= kLoadWarp0 && warp < kConvWarp0) {
     // ------------------------------------------------------------ loaders
@@ -424,7 +429,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     : swz128(row, c);
     const bool taps = p.a_mode == kALoadIm2colTaps;
     int kb = 0;
-    for (int item = 0; item < total_items; ++item) {
+    for (int item = 0; item < (direct ? 0 : total_items); ++item) {
       const int s = item % S1;
       const int a = item % S2;
       bool ok = mbar_wait(s1_full(s), (item / S1) & 1, abort_flag, p.status);
@@ -535,7 +540,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // the converters arrive on t_full only after they saw the stage's TMA
         // (A and B) complete on s1_full and wrote its A operands
-        if (!mbar_wait(t_full(a), pa, abort_flag, p.status)) break;
+        if (direct ? !mbar_wait(s1_full(s), (item / S1) & 1, abort_flag, p.status)
+                   : !mbar_wait(t_full(a), pa, abort_flag, p.status))
+          break;
         tc_fence_after();
         const uint32_t ahi = tmem_base + L::kACol0 + a * L::kAStageCols;  // 3xTF32: A hi | lo
         const uint32_t alo = ahi + kBK;
@@ -849,12 +856,16 @@ template <int PREC, int BN, int EG, int NB, int AIO = 0>
 int launch3_t(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap& lo,
               const CUtensorMap& am, const CUtensorMap& am2, int num_sms, cudaStream_t st) {
   using L = Layout<PREC, BN, EG, NB, AIO>;
-  static bool attr_set = false;
-  if (!attr_set) {
+  // the shared-memory opt-in is a per-device attribute of the kernel
+  constexpr int kMaxDevices = 64;
+  static bool attr_set[kMaxDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return (int)cudaErrorInvalidDevice;
+  if (!attr_set[dev]) {
     cudaError_t e = cudaFuncSetAttribute(igemm_tc3_kernel<PREC, BN, EG, NB, AIO>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
     if (e != cudaSuccess) return (int)e;
-    attr_set = true;
+    attr_set[dev] = true;
   }
   CUtensorMap ym{}, rm{};
   int er = encode_out_map(p.y, p.Nc, p.M, p.batches, p.ldy, p.y_bstride, EG, L::kOes, &ym);
