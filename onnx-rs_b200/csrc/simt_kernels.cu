@@ -169,6 +169,119 @@ __global__ void conv_grouped_v4_kernel(const float* __restrict__ x, int H, int W
   }
 }
 
+// Grouped 3x3 convolution (dilation 1, stride S) over output-row segments: a
+// thread computes P consecutive output pixels of one row for 4 output channels
+// of one group.  Per filter row and input-channel quadruple it loads the
+// (P-1)*S+3 input vectors its segment touches once into registers, then for
+// each of the 3 taps and 4 channels reads one 16-byte weight vector from shared
+// memory and applies it to all P pixels (4P FMAs per shared-memory load; the
+// per-pixel kernel above does 4).  A block works on one slice of CB output
+// channels and keeps only that slice's weights, [tap][ci][co in slice], in
+// shared memory, so that wide groups (e.g. 32 groups of 32 channels) fit.
+// Sums over (kh, ci, kw) in fp32.
+template <int S, int P>
+__global__ void __launch_bounds__(256, 2)
+    conv_grouped_row_kernel(const float* __restrict__ x, int H, int W, int Cs,
+                            const float* __restrict__ w, int CB, int CO, int cg, int cog, int ph,
+                            int pw, int OH, int OW, int nseg, unsigned per_slice,
+                            int blocks_per_slice, const float* __restrict__ scale,
+                            const float* __restrict__ shift, const float* __restrict__ res, int relu,
+                            float* __restrict__ y) {
+  extern __shared__ float ws[];
+  const int slice = blockIdx.x / blocks_per_slice, bis = blockIdx.x % blocks_per_slice;
+  const int cb0 = slice * CB;
+  // the slice's OIHW weights are one contiguous run: each thread copies whole
+  // 9-tap filters (coalesced across the warp) into the [tap][ci][co] layout
+  const float* wsl = w + (long long)cb0 * cg * 9;
+  for (int j = threadIdx.x; j < CB * cg; j += blockDim.x) {
+    const int c = j / cg, ci = j - c * cg;
+#pragma unroll
+    for (int tap = 0; tap < 9; ++tap) ws[(tap * cg + ci) * CB + c] = __ldg(wsl + j * 9 + tap);
+  }
+  __syncthreads();
+  constexpr int NI = (P - 1) * S + 3;
+  const unsigned CB4 = CB / 4;
+  const int Cs4 = Cs / 4;
+  for (unsigned idx = bis * blockDim.x + threadIdx.x; idx < per_slice;
+       idx += blocks_per_slice * blockDim.x) {
+    const int c0 = (int)(idx % CB4) * 4;
+    unsigned t = idx / CB4;
+    const int seg = (int)(t % (unsigned)nseg);
+    t /= (unsigned)nseg;
+    const int oh = (int)(t % (unsigned)OH);
+    const unsigned n = t / (unsigned)OH;
+    const int co0 = cb0 + c0;
+    const int ow0 = seg * P, iw0 = ow0 * S - pw;
+    const float4* xb = reinterpret_cast<const float4*>(x + (size_t)n * H * W * Cs + (co0 / cog) * cg);
+    float acc[P][4];
+#pragma unroll
+    for (int p = 0; p < P; ++p) acc[p][0] = acc[p][1] = acc[p][2] = acc[p][3] = 0.f;
+    // the lanes of a warp usually share one row segment, so these branches are uniform
+    const bool interior = iw0 >= 0 && iw0 + NI <= W;
+    for (int c4 = 0; c4 < cg / 4; ++c4) {
+      for (int r = 0; r < 3; ++r) {
+        const int ih = oh * S - ph + r;
+        if ((unsigned)ih >= (unsigned)H) continue;  // zero rows add nothing
+        const float4* xrow = xb + ((size_t)ih * W + iw0) * Cs4 + c4;
+        float4 xin[NI];
+        if (interior) {
+#pragma unroll
+          for (int i = 0; i < NI; ++i) xin[i] = __ldg(xrow + i * Cs4);
+        } else {
+#pragma unroll
+          for (int i = 0; i < NI; ++i)
+            xin[i] = (unsigned)(iw0 + i) < (unsigned)W ? __ldg(xrow + i * Cs4)
+                                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        const float* wr = ws + (r * 3 * cg + 4 * c4) * CB + c0;
+#pragma unroll
+        for (int q = 0; q < 3; ++q)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float4 wv = *reinterpret_cast<const float4*>(wr + (q * cg + e) * CB);
+#pragma unroll
+            for (int p = 0; p < P; ++p) {
+              const float4 xv = xin[p * S + q];
+              const float xs = e == 0 ? xv.x : e == 1 ? xv.y : e == 2 ? xv.z : xv.w;
+              acc[p][0] = fmaf(xs, wv.x, acc[p][0]);
+              acc[p][1] = fmaf(xs, wv.y, acc[p][1]);
+              acc[p][2] = fmaf(xs, wv.z, acc[p][2]);
+              acc[p][3] = fmaf(xs, wv.w, acc[p][3]);
+            }
+          }
+      }
+    }
+    // epilogue: y = acc * scale + shift (+ res) (Relu), 16-byte vectors
+    const float4 sc = scale ? __ldg(reinterpret_cast<const float4*>(scale + co0)) : make_float4(1.f, 1.f, 1.f, 1.f);
+    const float4 sf = shift ? __ldg(reinterpret_cast<const float4*>(shift + co0)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    const long long o0 = (((long long)n * OH + oh) * OW + ow0) * CO + co0;
+#pragma unroll
+    for (int p = 0; p < P; ++p) {
+      if (ow0 + p >= OW) break;
+      const long long o = o0 + (long long)p * CO;
+      float4 v = make_float4(fmaf(acc[p][0], sc.x, sf.x), fmaf(acc[p][1], sc.y, sf.y),
+                             fmaf(acc[p][2], sc.z, sf.z), fmaf(acc[p][3], sc.w, sf.w));
+      if (res) {
+        const float4 rv = __ldg(reinterpret_cast<const float4*>(res + o));
+        v.x += rv.x, v.y += rv.y, v.z += rv.z, v.w += rv.w;
+      }
+      if (relu) v = make_float4(fmaxf(v.x, 0.f), fmaxf(v.y, 0.f), fmaxf(v.z, 0.f), fmaxf(v.w, 0.f));
+      *reinterpret_cast<float4*>(y + o) = v;
+    }
+  }
+}
+
+namespace {
+// Output-channel slice of the row kernel: the widest divisor of CO that is a
+// multiple of 4 and whose [tap][ci][co] weights fit 64 KB of shared memory.
+int grouped_row_slice(int CO, int cg) {
+  const long long per_co = (long long)cg * 9 * sizeof(float);
+  for (int cb = CO; cb >= 4; --cb)
+    if (CO % cb == 0 && cb % 4 == 0 && cb * per_co <= 64 * 1024) return cb;
+  return 0;
+}
+}  // namespace
+
 int conv_direct_launch(const float* x, int N, int H, int W, int C, int Cs, const float* w, int CO,
                        int KH, int KW, int sh, int sw, int ph, int pw, int dh, int dw, int group, int OH,
                        int OW, const float* scale, const float* shift, const float* res, int relu,
@@ -178,6 +291,38 @@ int conv_direct_launch(const float* x, int N, int H, int W, int C, int Cs, const
   const int cg = C / group, cog = CO / group;
   const size_t wbytes = (size_t)CO * cg * KH * KW * sizeof(float);
   auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+  const bool al = a16(x) && a16(y) && (!res || a16(res)) && (!scale || a16(scale)) &&
+                  (!shift || a16(shift));
+  // 3x3 stride 1 / 2 (ResNeXt's grouped convolutions): row segments of 7 pixels
+  constexpr int kSeg = 7;
+  if (group > 1 && KH == 3 && KW == 3 && dh == 1 && dw == 1 && sh == sw && (sh == 1 || sh == 2) &&
+      cg % 4 == 0 && cog % 4 == 0 && Cs % 4 == 0 && al) {
+    const int CB = grouped_row_slice(CO, cg);
+    const int nseg = (OW + kSeg - 1) / kSeg;
+    const long long per_slice = (long long)N * OH * nseg * (CB / 4);
+    if (CB > 0 && per_slice < (1ll << 31) && (long long)N * H * W * Cs < (1ll << 40)) {
+      const int nslices = CO / CB;
+      // persistent: one wave of resident blocks in all, each staging its
+      // slice's weights once
+      auto kern = sh == 1 ? conv_grouped_row_kernel<1, kSeg> : conv_grouped_row_kernel<2, kSeg>;
+      static int resident[2] = {0, 0};  // blocks per SM (same for every B200)
+      int& occ = resident[sh - 1];
+      const size_t sbytes = (size_t)CB * cg * 9 * sizeof(float);
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024) != cudaSuccess)
+        return (int)cudaGetLastError();
+      if (!occ && cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, 256, 64 * 1024) != cudaSuccess)
+        return (int)cudaGetLastError();
+      int sms = 148, dev = 0;
+      cudaGetDevice(&dev);
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      const int bps = (int)std::max<long long>(
+          1, std::min<long long>((per_slice + 255) / 256,
+                                 ((long long)sms * std::max(occ, 1) + nslices - 1) / nslices));
+      kern<<<nslices * bps, 256, sbytes, st>>>(x, H, W, Cs, w, CB, CO, cg, cog, ph, pw, OH, OW, nseg,
+                                               (unsigned)per_slice, bps, scale, shift, res, relu, y);
+      return (int)cudaGetLastError();
+    }
+  }
   if (group > 1 && cg % 4 == 0 && cog % 4 == 0 && Cs % 4 == 0 && wbytes <= 96 * 1024 && a16(x) &&
       a16(y) && (!res || a16(res)) && total / 4 < (1ll << 31)) {
     const long long total4 = total / 4;

@@ -68,7 +68,8 @@ SWEEP = [
     ("1x1_256_14", 256, 256, 14, 1, 0, 1, 1), ("3x3_256_14", 256, 256, 14, 3, 1, 1, 1),
     ("1x1_512_7", 512, 512, 7, 1, 0, 1, 1), ("3x3_512_7", 512, 512, 7, 3, 1, 1, 1),
     ("1x1_256to1024_14", 256, 1024, 14, 1, 0, 1, 1),
-    ("3x3_g32_128_28", 128, 128, 28, 3, 1, 1, 32),
+    ("3x3_g32_128_28", 128, 128, 28, 3, 1, 1, 32), ("3x3_g32_256_14", 256, 256, 14, 3, 1, 1, 32),
+    ("3x3_g32_1024_7", 1024, 1024, 7, 3, 1, 1, 32),
     ("3x3_d2_256_28", 256, 256, 28, 3, 2, 2, 1),
 ]
 

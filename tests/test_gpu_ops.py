@@ -52,6 +52,12 @@ SMALL = [
     ("grouped", (2, 32, 10, 10), 32, 3, 1, 1, 1, 8),
     ("grouped_cg8_s2", (2, 32, 9, 11), 16, 3, 2, 1, 1, 4),
     ("grouped_cg3", (1, 12, 8, 8), 12, 3, 1, 1, 1, 4),
+    # grouped 3x3 over row segments: segments past the row end, weight slices
+    # narrower than CO, stride 2, no padding, two output channels per input one
+    ("grouped_cg32_sliced", (2, 256, 9, 13), 256, 3, 1, 1, 1, 8),
+    ("grouped_g32_s2_odd", (3, 128, 15, 17), 128, 3, 2, 1, 1, 32),
+    ("grouped_pad0", (2, 64, 12, 12), 64, 3, 1, 0, 1, 16),
+    ("grouped_cog8", (2, 32, 8, 30), 64, 3, 1, 1, 1, 8),
     ("c5_odd_channels", (2, 5, 9, 9), 12, 3, 1, 1, 1, 1),
     ("c3_dil2_s2", (2, 3, 17, 19), 16, 3, 2, 2, 2, 1),
     ("c6_5x5_s2", (1, 6, 21, 18), 24, 5, 2, 2, 1, 1),
