@@ -165,6 +165,23 @@ int resolve_conv_desc(onnxb200_handle* h, const onnxb200_conv_desc* in, onnxb200
   return ONNXB200_OK;
 }
 
+// Tile width and K split of a tensor-core plan (p->d, num_kb, a_bf16 set):
+// K splits for fp32-activation problems with too few output tiles.
+static void choose_tiling(onnxb200_handle* h, onnxb200_conv_plan* p, bool residual) {
+  IgemmParams q{};
+  q.M = (int)(p->d.n * p->oh * p->ow);
+  q.Nc = (int)p->d.c_out;
+  q.batches = 1;
+  q.num_kb = p->num_kb;
+  q.a_bf16 = p->a_bf16;
+  q.res = residual ? reinterpret_cast<const float*>(p) : nullptr;  // a flag here, never read
+  int bn = 128, ks = 1;
+  igemm_pick_split(q, p->prec, h->num_sms, &bn, &ks);
+  p->bn = bn;
+  p->ksplit = ks;
+  p->split_bytes = ks > 1 ? (size_t)ks * q.M * q.Nc * sizeof(float) : 0;
+}
+
 void conv_plan_free(onnxb200_conv_plan* p) {
   (void)p;
 }
@@ -192,7 +209,7 @@ int conv_plan_init(onnxb200_handle* h, const onnxb200_conv_desc* din, int cs_in,
   p->out_bf16 = out_bf16;
   const int CO = (int)d.c_out;
   size_t need = 0;
-  size_t off_hi = 0, off_lo = 0, off_scale = 0, off_shift = 0, off_w = 0;
+  size_t off_hi = 0, off_lo = 0, off_scale = 0, off_shift = 0, off_w = 0, off_split = 0;
   p->pairs = p->use_tc && !a_bf16 && cs_in == 4 && d.stride_w == 2 && d.dil_w == 1 &&
              d.w % 2 == 0 && d.kw > 1;
   const int kwp = (int)((d.kw + (d.pad_left & 1) + 1) / 2);  // pair taps
@@ -200,6 +217,7 @@ int conv_plan_init(onnxb200_handle* h, const onnxb200_conv_desc* din, int cs_in,
     p->K = p->pairs ? (int)(d.kh * kwp * 8) : (int)(d.kh * d.kw * cs_in);
     p->kpad = igemm_kpad(p->K, p->prec, a_bf16);
     p->num_kb = p->kpad / igemm_block_k(p->prec, a_bf16);
+    choose_tiling(h, p, (d.epilogue & ONNXB200_EPI_RESIDUAL) != 0);
     const size_t esz = p->prec == kPrecBF16 ? 2 : 4;
     const size_t wbytes = align_up((size_t)CO * p->kpad * esz);
     off_hi = need;
@@ -209,6 +227,10 @@ int conv_plan_init(onnxb200_handle* h, const onnxb200_conv_desc* din, int cs_in,
       need += wbytes;
     }
     p->weight_bytes = (int64_t)need;
+    if (!scratch && !scratch_used && p->split_bytes) {  // op-level plans own their K-split buffer
+      off_split = need;
+      need += align_up(p->split_bytes);
+    }
   } else {
     off_w = need;
     need += align_up((size_t)CO * (d.c / d.group) * d.kh * d.kw * sizeof(float));
@@ -240,20 +262,17 @@ int conv_plan_init(onnxb200_handle* h, const onnxb200_conv_desc* din, int cs_in,
   p->w_oihw = nullptr;
   p->scale = p->shift = nullptr;
   cudaStream_t st = h->stream;
+  p->split_ws = nullptr;
   if (p->use_tc) {
     p->w_hi = basep + off_hi;
     if (p->prec == kPrec3xTF32) p->w_lo = basep + off_lo;
+    if (off_split) p->split_ws = reinterpret_cast<float*>(basep + off_split);
     // OIHW element (co, ci, r, s) -> k = (r*KW + s)*cs_in + ci
     rc = pack_b_launch(w, CO, p->K, p->kpad, cs_in, (int)d.c, CO, 0, d.c * d.kh * d.kw, 1,
                        d.kh * d.kw, p->prec, p->w_hi, p->w_lo, st, p->pairs ? (int)d.kw : 0,
                        (int)(d.pad_left & 1));
     h->launches++;
     if (rc) return cuda_check(h, (cudaError_t)rc, "weight packing");
-    IgemmParams q{};
-    q.M = (int)(d.n * p->oh * p->ow);
-    q.Nc = CO;
-    q.batches = 1;
-    p->bn = igemm_pick_bn(q, p->prec, h->num_sms);
     const int bk = igemm_block_k(p->prec, a_bf16);
     rc = encode_weight_map(h, &p->tm_hi, p->w_hi, CO, p->kpad, p->prec, p->bn, bk);
     if (rc) return rc;
@@ -281,7 +300,7 @@ int conv_plan_init(onnxb200_handle* h, const onnxb200_conv_desc* din, int cs_in,
 }
 
 int conv_plan_exec_nhwc(onnxb200_handle* h, const onnxb200_conv_plan* p, const float* x,
-                        const float* residual, float* y) {
+                        const float* residual, float* y, float* split_ws) {
   const onnxb200_conv_desc& d = p->d;
   const bool relu = (d.epilogue & ONNXB200_EPI_RELU) != 0;
   const float* res = (d.epilogue & ONNXB200_EPI_RESIDUAL) ? residual : nullptr;
@@ -335,7 +354,10 @@ int conv_plan_exec_nhwc(onnxb200_handle* h, const onnxb200_conv_plan* p, const f
       const int er = encode_a_map(q, rows, &am);
       if (er) return set_error(h, ONNXB200_ERR_EXECUTION, "Conv: A tensor map encode failed: " + std::to_string(er));
     }
-    rc = igemm_launch(q, p->tm_hi, p->tm_lo, am, am, p->prec, p->bn, h->num_sms, h->stream);
+    float* ws = split_ws ? split_ws : p->split_ws;
+    rc = igemm_launch_split(q, ws ? p->ksplit : 1, ws, p->tm_hi, p->tm_lo, am, am, p->prec, p->bn, h->num_sms,
+                            h->stream);
+    if (ws && p->ksplit > 1) h->launches++;  // the reduction pass
   } else {
     rc = conv_direct_launch(x, (int)d.n, (int)d.h, (int)d.w, (int)d.c, p->cs_in, p->w_oihw,
                             (int)d.c_out, (int)d.kh, (int)d.kw, (int)d.stride_h, (int)d.stride_w,
@@ -379,6 +401,7 @@ int conv_dual_plan_init(onnxb200_handle* h, const onnxb200_conv_desc* d1, int cs
   p->K = (int)(a.c + r2.c);
   p->kpad = p->K;
   p->num_kb = p->K / bk;
+  choose_tiling(h, p, false);
   const size_t esz = p->prec == kPrecBF16 ? 2 : 4;
   const size_t wbytes = align_up((size_t)CO * p->kpad * esz);
   size_t need = wbytes * (p->prec == kPrec3xTF32 ? 2 : 1);
@@ -391,6 +414,8 @@ int conv_dual_plan_init(onnxb200_handle* h, const onnxb200_conv_desc* d1, int cs
   const size_t off_t2 = need;
   need += align_up(CO * sizeof(float));
   p->weight_bytes = (int64_t)need;
+  const size_t off_split = (!scratch && !scratch_used && p->split_bytes) ? need : 0;
+  if (off_split) need += align_up(p->split_bytes);
   if (!scratch && scratch_used) {
     *scratch_used = need;
     return ONNXB200_OK;
@@ -413,6 +438,7 @@ int conv_dual_plan_init(onnxb200_handle* h, const onnxb200_conv_desc* d1, int cs
   float* s2 = reinterpret_cast<float*>(basep + off_s2);
   float* t1 = reinterpret_cast<float*>(basep + off_t1);
   float* t2 = reinterpret_cast<float*>(basep + off_t2);
+  p->split_ws = off_split ? reinterpret_cast<float*>(basep + off_split) : nullptr;
   // each branch's BatchNormalization as scale / shift; the scales go into the
   // packed weights, the shifts are added: y = (s1 W1) x1 + (s2 W2) x2 + t1 + t2
   rc = bn_fold_launch(bn1.scale, bn1.bias, bn1.mean, bn1.var, bn1.conv_bias, bn1.eps, CO, s1, t1, st);
@@ -423,11 +449,6 @@ int conv_dual_plan_init(onnxb200_handle* h, const onnxb200_conv_desc* d1, int cs
   if (rc) return cuda_check(h, (cudaError_t)rc, "two-source weight packing");
   p->scale = nullptr;
   p->shift = t1;
-  IgemmParams q{};
-  q.M = (int)(a.n * p->oh * p->ow);
-  q.Nc = CO;
-  q.batches = 1;
-  p->bn = igemm_pick_bn(q, p->prec, h->num_sms);
   rc = encode_weight_map(h, &p->tm_hi, p->w_hi, CO, p->kpad, p->prec, p->bn, bk);
   if (rc) return rc;
   return encode_weight_map(h, &p->tm_lo, p->w_lo ? p->w_lo : p->w_hi, CO, p->kpad, p->prec, p->bn, bk);
@@ -444,7 +465,7 @@ bool dual_conv_supported(const onnxb200_conv_desc& a, int cs1, const onnxb200_co
 }
 
 int conv_dual_exec_nhwc(onnxb200_handle* h, const onnxb200_conv_plan* p, const float* x1, const float* x2,
-                        float* y) {
+                        float* y, float* split_ws) {
   const onnxb200_conv_desc& d = p->d;
   if (!p->dual) return set_error(h, ONNXB200_ERR_INVALID_ARGUMENT, "Conv: not a two-source plan");
   if (d.n == 0) return ONNXB200_OK;
@@ -489,8 +510,10 @@ int conv_dual_exec_nhwc(onnxb200_handle* h, const onnxb200_conv_plan* p, const f
   int er = encode_a_map(q, (int)d.n * q.Hin * q.Win, &am);
   if (!er) er = encode_a_map(v, q.a_mode2 == kALoadTma2d ? (int)d.n * q.H2 * q.W2 : (int)d.n, &am2);
   if (er) return set_error(h, ONNXB200_ERR_EXECUTION, "Conv: A tensor map encode failed: " + std::to_string(er));
-  const int rc = igemm_launch(q, p->tm_hi, p->tm_lo, am, am2, p->prec, p->bn, h->num_sms, h->stream);
-  h->launches++;
+  float* ws = split_ws ? split_ws : p->split_ws;
+  const int rc = igemm_launch_split(q, ws ? p->ksplit : 1, ws, p->tm_hi, p->tm_lo, am, am2, p->prec, p->bn,
+                                    h->num_sms, h->stream);
+  h->launches += (ws && p->ksplit > 1) ? 2 : 1;
   if (rc) return cuda_check(h, (cudaError_t)rc, "Conv launch");
   return ONNXB200_OK;
 }
@@ -524,7 +547,15 @@ int gemm_tc_run(onnxb200_handle* h, const GemmCall& c, const void* b_hi, const v
   q.ldr = c.ldr;
   q.relu = c.relu;
   q.status = h->d_status;
-  const int bn = igemm_pick_bn(q, prec, h->num_sms);
+  int bn = igemm_pick_bn(q, prec, h->num_sms), ks = 1;
+  if (c.split_ws) {
+    int b2 = bn, k2 = 1;
+    igemm_pick_split(q, prec, h->num_sms, &b2, &k2);
+    if (k2 > 1 && (size_t)k2 * q.M * q.Nc * sizeof(float) <= c.split_bytes) {
+      bn = b2;
+      ks = k2;
+    }
+  }
   q.m_tiles = (q.M + 127) / 128;
   q.n_tiles = (q.Nc + bn - 1) / bn;
   CUtensorMap thi, tlo;
@@ -538,10 +569,23 @@ int gemm_tc_run(onnxb200_handle* h, const GemmCall& c, const void* b_hi, const v
     const int er = encode_a_map(q, c.a_rows > 0 ? c.a_rows : c.M, &am);
     if (er) return set_error(h, ONNXB200_ERR_EXECUTION, "GEMM: A tensor map encode failed: " + std::to_string(er));
   }
-  rc = igemm_launch(q, thi, tlo, am, am, prec, bn, h->num_sms, h->stream);
-  h->launches++;
+  rc = igemm_launch_split(q, ks, c.split_ws, thi, tlo, am, am, prec, bn, h->num_sms, h->stream);
+  h->launches += ks > 1 ? 2 : 1;
   if (rc) return cuda_check(h, (cudaError_t)rc, "GEMM launch");
   return ONNXB200_OK;
+}
+
+size_t gemm_split_bytes(const onnxb200_handle* h, int M, int N, int kpad, int prec, bool residual) {
+  if (prec == kPrecFP32) return 0;
+  IgemmParams q{};
+  q.M = M;
+  q.Nc = N;
+  q.batches = 1;
+  q.num_kb = kpad / igemm_block_k(prec);
+  q.res = residual ? reinterpret_cast<const float*>(h) : nullptr;  // a flag here, never read
+  int bn = 128, ks = 1;
+  igemm_pick_split(q, prec, h->num_sms, &bn, &ks);
+  return ks > 1 ? (size_t)ks * M * N * sizeof(float) : 0;
 }
 
 }  // namespace ob2

@@ -140,6 +140,9 @@ struct onnxb200_graph {
   size_t weight_bytes = 0;
   uint8_t* init = nullptr;           // device copies of initializers + small tables
   size_t init_bytes = 0;
+  // K-split partial sums of the steps that split (one at a time: steps run in order)
+  float* split_ws = nullptr;
+  size_t split_bytes = 0;
   int n_nodes_in = 0, n_fused = 0;
   int64_t kernels_per_run = -1;
   // CUDA graph state
@@ -417,6 +420,7 @@ static void destroy_graph(onnxb200_graph* g) {
   if (g->cg) cudaGraphDestroy(g->cg);
   if (g->arena) cudaFree(g->arena);
   if (g->weights) cudaFree(g->weights);
+  if (g->split_ws) cudaFree(g->split_ws);
   if (g->init) cudaFree(g->init);
   for (void* p : g->dev_in) if (p) cudaFree(p);
   for (void* p : g->dev_out) if (p) cudaFree(p);
@@ -1091,6 +1095,21 @@ extern "C" int onnxb200_graph_build(onnxb200_handle* h, const onnxb200_node* nod
     int rc = init_plan(pconv[i], g->weights + plan_off[i], wtotal - plan_off[i], &used);
     if (rc) { destroy_graph(g); return rc; }
   }
+  // one K-split buffer for every step that splits (a few late layers and the
+  // classifier at small batches; none at large ones)
+  {
+    size_t sb = 0;
+    for (const onnxb200_conv_plan& p : g->plans)
+      if (p.use_tc && p.ksplit > 1) sb = std::max(sb, p.split_bytes);
+    for (const GemmPlan& gp : g->gemms)
+      if (gp.batches == 1 && gp.aoff_off == SIZE_MAX && gp.brow_off == SIZE_MAX)
+        sb = std::max(sb, gemm_split_bytes(h, gp.M, gp.N, gp.kpad, gp.prec, false));
+    if (sb) {
+      e = cudaMalloc(reinterpret_cast<void**>(&g->split_ws), sb);
+      if (e != cudaSuccess) return bail(ONNXB200_ERR_RESOURCE_EXHAUSTED, "graph: K-split buffer allocation failed");
+      g->split_bytes = sb;
+    }
+  }
   for (size_t i = 0; i < pgemm.size(); ++i) {
     const PendingGemm& pg = pgemm[i];
     GemmPlan& gp = g->gemms[pg.gp];
@@ -1225,9 +1244,10 @@ static int run_steps(onnxb200_graph* g, const float* const* uin, float* const* u
       case kConv: {
         const onnxb200_conv_plan& p = g->plans[s.conv];
         if (p.dual)
-          rc = conv_dual_exec_nhwc(h, &p, T(s.in[0]), T(s.in[1]), T(s.out));
+          rc = conv_dual_exec_nhwc(h, &p, T(s.in[0]), T(s.in[1]), T(s.out), g->split_ws);
         else
-          rc = conv_plan_exec_nhwc(h, &p, T(s.in[0]), s.in.size() > 1 ? T(s.in[1]) : nullptr, T(s.out));
+          rc = conv_plan_exec_nhwc(h, &p, T(s.in[0]), s.in.size() > 1 ? T(s.in[1]) : nullptr, T(s.out),
+                                   g->split_ws);
         if (rc) return rc;
         break;
       }
@@ -1313,6 +1333,8 @@ static int run_steps(onnxb200_graph* g, const float* const* uin, float* const* u
           h->launches++;
           if (c.b_row) return fail(h, ONNXB200_ERR_UNSUPPORTED, "batched MatMul in fp32 CUDA-core mode");
         } else {
+          c.split_ws = g->split_ws;
+          c.split_bytes = g->split_bytes;
           rc = gemm_tc_run(h, c, g->weights + gp.w_hi_off,
                            gp.prec == kPrec3xTF32 ? g->weights + gp.w_lo_off : nullptr, gp.b_rows, gp.kpad,
                            gp.prec);

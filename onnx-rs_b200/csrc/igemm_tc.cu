@@ -62,7 +62,7 @@ int igemm_launch(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap&
   auto mis = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) != 0; };
   if (!p.x || !p.y || mis(p.x) || mis(p.y) || (p.res && mis(p.res)) || (p.scale && mis(p.scale)) ||
       (p.shift && mis(p.shift)) || p.Cs % 4 || p.Nc % 4 || p.ldy % 4 || (p.res && p.ldr % 4) ||
-      p.y_bstride % 4 || p.num_kb <= 0 || (p.batches > 1 && !p.a_off && p.M % 4))
+      p.y_bstride % 4 || p.num_kb <= 0 || (p.batches > 1 && p.ksplit <= 1 && !p.a_off && p.M % 4))
     return (int)cudaErrorMisalignedAddress;
   // two sources: source 1 a [pixels][Cs] matrix of whole k-blocks, source 2 a
   // 1x1 convolution of whole k-blocks at the same output pixels
@@ -70,8 +70,13 @@ int igemm_launch(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap&
   // bf16 activations: whole taps per k-block through TMA, no padding
   if (p.a_bf16 && (p.a_mode == kALoadGather || p.a_mode == kALoadIm2colTaps || p.Cs % bk || p.K % bk))
     return (int)cudaErrorInvalidValue;
+  // K split: `ksplit` batches over one A and B, whole k-blocks per slice
+  if (p.ksplit > 1 && (p.batches != p.ksplit || p.a_off || p.b_row || p.res || p.scale || p.shift ||
+                       p.relu || p.out_bf16 || p.num_kb % p.ksplit))
+    return (int)cudaErrorInvalidValue;
   if (p.kb_split &&
-      (p.a_mode != kALoadTma2d || p.Cs != p.kb_split * bk || p.batches != 1 || p.a_off || !p.x2 ||
+      (p.a_mode != kALoadTma2d || p.Cs != p.kb_split * bk || p.batches != (p.ksplit > 1 ? p.ksplit : 1) ||
+       p.a_off || !p.x2 ||
        mis(p.x2) || p.Cs2 % bk || p.s2 < 1 || p.num_kb != p.kb_split + p.Cs2 / bk ||
        (p.a_mode2 != kALoadTma2d && p.a_mode2 != kALoadIm2col) ||
        (p.a_mode2 == kALoadTma2d && (p.s2 != 1 || p.H2 != p.OH || p.W2 != p.OW))))
@@ -79,6 +84,73 @@ int igemm_launch(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap&
   if (precision == kPrec3xTF32 || precision == kPrecTF32 || precision == kPrecBF16)
     return igemm3_launch(p, hi, lo, am, am2, precision, bn, num_sms, st);
   return (int)cudaErrorInvalidValue;
+}
+
+int igemm_launch_split(const IgemmParams& p, int ksplit, float* ws, const CUtensorMap& hi,
+                       const CUtensorMap& lo, const CUtensorMap& am, const CUtensorMap& am2, int precision,
+                       int bn, int num_sms, cudaStream_t st) {
+  if (ksplit <= 1) return igemm_launch(p, hi, lo, am, am2, precision, bn, num_sms, st);
+  if (!ws || (reinterpret_cast<uintptr_t>(ws) & 15) || p.batches != 1 || p.a_off || p.b_row || p.a_bf16 ||
+      p.num_kb % ksplit)
+    return (int)cudaErrorInvalidValue;
+  // slice b's raw sums -> ws[b][M][Nc]
+  IgemmParams q = p;
+  q.ksplit = ksplit;
+  q.batches = ksplit;
+  q.y = ws;
+  q.ldy = p.Nc;
+  q.y_bstride = (long long)p.M * p.Nc;
+  q.scale = q.shift = q.res = nullptr;
+  q.relu = 0;
+  q.out_bf16 = 0;
+  int rc = igemm_launch(q, hi, lo, am, am2, precision, bn, num_sms, st);
+  if (rc) return rc;
+  return splitk_reduce_launch(ws, ksplit, p.M, p.Nc, p.y, p.ldy, p.scale, p.shift, p.res, p.ldr, p.relu,
+                              p.out_bf16, st);
+}
+
+void igemm_pick_split(const IgemmParams& p, int precision, int num_sms, int* bn, int* ksplit) {
+  const int bn0 = igemm_pick_bn(p, precision, num_sms);
+  *bn = bn0;
+  *ksplit = 1;
+  if (p.batches != 1 || p.a_off || p.b_row || p.a_bf16 || p.num_kb < 8 || num_sms <= 0) return;
+  // modelled time in units of one k-block of a 128-column tile; a 64-column
+  // tile's k-block costs ~0.8 of it (its MMAs are half as long, the operand
+  // round trip is not)
+  const double kb_us = precision == kPrec3xTF32 ? 0.8 : 0.5;
+  const long long mt = (p.M + kBM - 1) / kBM;
+  auto cost = [&](int b, int s) {
+    const long long tiles = mt * ((p.Nc + b - 1) / b);
+    const long long waves = (tiles * s + num_sms - 1) / num_sms;
+    double c = (double)waves * (p.num_kb / s) * (b == 64 ? 0.8 : 1.0);
+    if (s > 1) {  // reduction pass: read the s slices (from L2 when they fit it,
+                  // ~10 TB/s), read the residual and write y from / to HBM (~6 TB/s)
+      const double slice = (double)p.M * p.Nc * 4.0;
+      const double ws_gbs = s * slice <= 64e6 ? 10.0e6 : 6.0e6;  // bytes per us
+      c += (s * slice / ws_gbs + (1 + (p.res ? 1 : 0)) * slice / 6.0e6 + 2.0) / kb_us;
+    }
+    return c;
+  };
+  double best = cost(bn0, 1);
+  const double unsplit = best;
+  int best_bn = bn0, best_s = 1;
+  const int cands[2] = {bn0, (bn0 == 64 && p.Nc > 64 && precision != kPrecTF32) ? 128 : 0};
+  for (int b : cands) {
+    if (!b) continue;
+    for (int s = 2; s <= 16; ++s) {
+      if (p.num_kb % s || p.num_kb / s < 4) continue;
+      const double c = cost(b, s);
+      if (c < best) {
+        best = c;
+        best_bn = b;
+        best_s = s;
+      }
+    }
+  }
+  if (best_s > 1 && best < 0.9 * unsplit) {
+    *bn = best_bn;
+    *ksplit = best_s;
+  }
 }
 
 int pick_a_mode(const IgemmParams& p, int precision) {

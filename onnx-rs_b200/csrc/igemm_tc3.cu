@@ -214,10 +214,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(s1_full(s), p.a_mode == kALoadGather ? 128 : 1);
       mbar_init(s1_empty(s), 1);  // the MMA commit (the MMAs ran after the converters)
     }
-    for (int a = 0; a < S2; ++a) mbar_init(t_full(a), 128);
+    // one arrival per converter / epilogue warp (lane 0, after the warp has
+    // converged): 128 single-thread arrivals on one barrier serialise for ~1k
+    // cycles, which sat on the MMA thread's critical path
+    for (int a = 0; a < S2; ++a) mbar_init(t_full(a), 4);
     for (int b = 0; b < 2; ++b) {
       mbar_init(acc_full(b), 1);
-      mbar_init(acc_empty(b), kEpiThreads);
+      mbar_init(acc_empty(b), kEpiThreads / 32);
     }
     for (int w = 0; w < 4; ++w)
       for (int b = 0; b < NB; ++b) mbar_init(res_full(w, b), 1);
@@ -258,7 +261,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   };
   const int my_tiles =
       (blockIdx.x < total_tiles) ? (total_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-  const int total_items = my_tiles * p.num_kb;
+  // K split (p.ksplit > 1): the problem is run as p.ksplit "batches" over the
+  // same A and B, batch b taking k-blocks [b * nkb, (b + 1) * nkb) and storing
+  // its raw partial sums to its own slice of y
+  const int nkb = p.ksplit > 1 ? p.num_kb / p.ksplit : p.num_kb;
+  const int total_items = my_tiles * nkb;
   // The MMAs read A straight from the stage that TMA landed (TF32, bf16
   // activations) and no stage needs rewriting (no taps-mode boxes, no K
   // padding): the MMA thread waits for the stage itself and the converter warps
@@ -283,10 +290,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           // for its stage: the integer divisions take ~2k cycles, which would
           // otherwise sit between the stage's release and its refill, i.e. on
           // the round trip that bounds the K loop.
-          const int tj = item / p.num_kb;
-          const int kb = item - tj * p.num_kb;
+          const int tj = item / nkb;
           int b, mt, nt;
           tile_coords(blockIdx.x + tj * gridDim.x, b, mt, nt);
+          const int kb = item - tj * nkb + (p.ksplit > 1 ? b * nkb : 0);  // k-block in K
           const int k0 = kb * kBK;
           // A bytes of this k-block: taps beyond K (the zero-weight padding of
           // the last k-block) are not loaded; the converters zero them
@@ -359,10 +366,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int item = 0; item < total_items; ++item) {
         const int s = item % S1;
         if (!mbar_wait(s1_empty(s), ((item / S1) & 1) ^ 1, abort_flag, p.status)) break;
-        const int tj = item / p.num_kb;
-        const int kb = item - tj * p.num_kb;
+        const int tj = item / nkb;
         int b, mt, nt;
         tile_coords(blockIdx.x + tj * gridDim.x, b, mt, nt);
+        const int kb = item - tj * nkb + (p.ksplit > 1 ? b * nkb : 0);
         if (tj != cur_tile) {
           cur_tile = tj;
           xb = p.x + (p.a_off ? p.a_off[b] : 0ll);
@@ -428,23 +435,29 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ? (uint32_t)((4 * c / p.Cs) * kBM * p.Cs * 4 + row * p.Cs * 4 + (4 * c % p.Cs) * 4)
                     : swz128(row, c);
     const bool taps = p.a_mode == kALoadIm2colTaps;
-    int kb = 0;
+    int kb = 0, kbase = 0;
     for (int item = 0; item < (direct ? 0 : total_items); ++item) {
       const int s = item % S1;
       const int a = item % S2;
-      bool ok = mbar_wait(s1_full(s), (item / S1) & 1, abort_flag, p.status);
+      // decisions stay warp-uniform: lane 0 arrives for the whole warp
+      bool ok = __all_sync(0xffffffffu, mbar_wait(s1_full(s), (item / S1) & 1, abort_flag, p.status));
       if constexpr (L::kABf16) {
         // bf16 activations: the MMAs read the stage as it landed (whole taps of
         // 64-channel multiples, no K padding), so there is nothing to convert
         if (!ok) break;
-        mbar_arrive(t_full(a));
+        if (lane == 0) mbar_arrive(t_full(a));
         continue;
       }
       const uint32_t rbase = a_raw + s * L::kARaw;
       // k beyond K: padding of the last k-block (zero weights); never multiply
       // whatever the stage held there
-      const int kvalid = p.K - kb * kBK;
-      if (++kb == p.num_kb) kb = 0;
+      if (kb == 0 && p.ksplit > 1) {  // first k-block of a tile: its place in K
+        int b, mt, nt;
+        tile_coords(blockIdx.x + (item / nkb) * gridDim.x, b, mt, nt);
+        kbase = b * nkb;
+      }
+      const int kvalid = p.K - (kbase + kb) * kBK;
+      if (++kb == nkb) kb = 0;
       // TF32: the MMAs read the raw fp32 A from shared memory (the tensor core
       // uses the upper 19 bits of the container); the stage is only rewritten
       // when its layout is not the MMA's (taps mode) or padding must be zeroed.
@@ -480,7 +493,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         // the slot's previous use have completed (see the 3xTF32 case below)
         if (item >= S2) {
           const int prev = item - S2;
-          if (!mbar_wait(s1_empty(prev % S1), (prev / S1) & 1, abort_flag, p.status)) break;
+          if (!__all_sync(0xffffffffu, mbar_wait(s1_empty(prev % S1), (prev / S1) & 1, abort_flag, p.status)))
+            break;
         }
         uint32_t pk[kBK / 2];
 #pragma unroll
@@ -501,7 +515,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         // commit of item - S1, and commits complete in order.
         if (item >= S2) {
           const int prev = item - S2;
-          if (!mbar_wait(s1_empty(prev % S1), (prev / S1) & 1, abort_flag, p.status)) break;
+          if (!__all_sync(0xffffffffu, mbar_wait(s1_empty(prev % S1), (prev / S1) & 1, abort_flag, p.status)))
+            break;
         }
         uint32_t hl[kBK];
 #pragma unroll
@@ -516,7 +531,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
       }
       if (rewrite) fence_proxy_async_smem();  // the generic-proxy stores, visible to the tensor core
-      mbar_arrive(t_full(a));
+      __syncwarp();  // every lane's TMEM / shared-memory stores precede lane 0's arrival
+      if (lane == 0) mbar_arrive(t_full(a));
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
@@ -580,7 +596,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // converters wait for this commit before refilling the slot)
         tc_commit(s1_empty(s));
         issued = true;
-        const bool tile_end = ++kb == p.num_kb;
+        const bool tile_end = ++kb == nkb;
         if (tile_end) kb = 0;
         if (tile_end || (L::kPromote && kin + 1 == L::kChunkKB)) {
           tc_commit(acc_full(cb));
@@ -650,7 +666,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (p.res && lane == 0 && rows_in) {
         for (int g = 0; g < NB && g < ngroups; ++g) issue_res(grp + g, nt * BN + g * kEG, r0, b);
       }
-      const int nch = L::kPromote ? (p.num_kb + L::kChunkKB - 1) / L::kChunkKB : 1;
+      const int nch = L::kPromote ? (nkb + L::kChunkKB - 1) / L::kChunkKB : 1;
       for (int ch = 0; ch < nch; ++ch) {
         const int cb = L::kPromote ? (cc & 1) : (tj & 1);
         const uint32_t cpar = L::kPromote ? ((cc >> 1) & 1) : ((tj >> 1) & 1);
@@ -794,7 +810,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!last) tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(acc_empty(cb));
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acc_empty(cb));
         if (L::kPromote) ++cc;
       }
     }
@@ -905,12 +922,13 @@ int igemm3_launch(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap
   // their epilogue, which 32-column groups store faster)
   // Short K loops are bound by the epilogue's HBM traffic: four staging
   // buffers (more stores and residual loads in flight) instead of operand stages.
-  const bool short_k = p.num_kb <= kShortK;
+  const int kb_tile = p.ksplit > 1 ? p.num_kb / p.ksplit : p.num_kb;  // k-blocks per tile
+  const bool short_k = kb_tile <= kShortK;
   if (precision == kPrec3xTF32 && bn == 64)
     return short_k ? launch3_t<kPrec3xTF32, 64, 32, 4>(p, hi, lo, am, am2, num_sms, st)
                    : launch3_t<kPrec3xTF32, 64, 32, 2>(p, hi, lo, am, am2, num_sms, st);
   if (precision == kPrec3xTF32 && bn == 128)
-    return p.num_kb >= kLongK ? launch3_t<kPrec3xTF32, 128, 16, 2>(p, hi, lo, am, am2, num_sms, st)
+    return kb_tile >= kLongK ? launch3_t<kPrec3xTF32, 128, 16, 2>(p, hi, lo, am, am2, num_sms, st)
            : short_k          ? launch3_t<kPrec3xTF32, 128, 32, 4>(p, hi, lo, am, am2, num_sms, st)
                               : launch3_t<kPrec3xTF32, 128, 32, 2>(p, hi, lo, am, am2, num_sms, st);
   if (precision == kPrecTF32 && bn == 64)

@@ -57,6 +57,13 @@ struct onnxb200_conv_plan {
   onnxb200_conv_desc d2{};
   int cs2 = 0;
   int kb_split = 0;
+  // K split (igemm_launch_split) when the problem has too few output tiles to
+  // fill the GPU: `ksplit` slices, partial sums in a buffer of split_bytes --
+  // the plan's own (split_ws, op-level plans) or one the caller passes (graphs);
+  // with neither the plan runs unsplit.
+  int ksplit = 1;
+  size_t split_bytes = 0;
+  float* split_ws = nullptr;
 };
 
 namespace ob2 {
@@ -104,11 +111,12 @@ int conv_dual_plan_init(onnxb200_handle* h, const onnxb200_conv_desc* d1, int cs
                         const ConvBranchBN& bn2, onnxb200_conv_plan* p, void* scratch, size_t scratch_bytes,
                         size_t* scratch_used, bool a_bf16 = false, bool out_bf16 = false);
 int conv_dual_exec_nhwc(onnxb200_handle* h, const onnxb200_conv_plan* p, const float* x1, const float* x2,
-                        float* y);
+                        float* y, float* split_ws = nullptr);
 
 // Runs a plan on NHWC buffers (x channel stride p->cs_in, y / residual stride C_out).
+// split_ws (>= p->split_bytes, or null for the plan's own) holds K-split partial sums.
 int conv_plan_exec_nhwc(onnxb200_handle* h, const onnxb200_conv_plan* p, const float* x,
-                        const float* residual, float* y);
+                        const float* residual, float* y, float* split_ws = nullptr);
 
 // Plain GEMM on the tcgen05 core:  y[b] = A_b * B_b^T(packed) with epilogue.
 struct GemmCall {
@@ -126,9 +134,15 @@ struct GemmCall {
   const float* res = nullptr;
   int ldr = 0;
   int relu = 0;
+  // K-split buffer (may be null): used when a split is modelled faster and fits
+  float* split_ws = nullptr;
+  size_t split_bytes = 0;
 };
 int gemm_tc_run(onnxb200_handle* h, const GemmCall& c, const void* b_hi, const void* b_lo,
                 int b_rows, int kpad, int prec);
+// Bytes of K-split buffer a single-batch tensor-core GEMM of this shape would
+// use in gemm_tc_run (0 = it would not split).
+size_t gemm_split_bytes(const onnxb200_handle* h, int M, int N, int kpad, int prec, bool residual);
 
 inline int resolve_prec(const onnxb200_handle* h, int prec) {
   return prec < 0 ? h->opts.precision : prec;

@@ -63,6 +63,10 @@ SMALL = [
     ("c6_5x5_s2", (1, 6, 21, 18), 24, 5, 2, 2, 1, 1),
     ("c3_7x7_s2_even_w", (2, 3, 30, 28), 24, 7, 2, 3, 1, 1),
     ("c4_3x3_s2_p2_even_w", (1, 4, 18, 20), 16, 3, 2, 2, 1, 1),
+    # few output tiles, long K: the K loop runs as slices on more SMs, then a
+    # reduction pass applies the epilogue
+    ("ksplit_3x3_512_7", (2, 512, 7, 7), 512, 3, 1, 1, 1, 1),
+    ("ksplit_1x1_2048_7_odd_m", (3, 2048, 5, 7), 512, 1, 1, 0, 1, 1),
     # 4-channel inputs with outputs >= 64 wide: whole input rows per filter row
     ("rows_7x7_s2_b3", (3, 3, 160, 132), 64, 7, 2, 3, 1, 1),
     ("rows_5x5_s1_c4", (2, 4, 70, 80), 24, 5, 1, 2, 1, 1),
