@@ -536,80 +536,91 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
-    // One thread, one flat loop over this CTA's k-blocks with incremental ring
-    // indices: the MMA issue rate of this thread bounds the kernel.
+    // One thread issues every MMA of the CTA, walking its k-blocks with
+    // incremental ring indices: the issue rate of this thread bounds the kernel.
     constexpr uint32_t idesc = make_idesc(2, kBM, BN);
     constexpr uint32_t idesc2 = make_idesc(2, kBM, 2 * BN);  // stacked B (BN = 64)
     constexpr uint32_t idesc_bf = make_idesc(1, kBM, BN);    // bf16 x bf16
     if (lane == 0) {
-      bool issued = false;
+      bool issued = false, ok = true;
       uint32_t cc = 0;             // accumulation units started (chunks / tiles)
       int s = 0, a = 0;            // shared-memory stage, TMEM A slot
       uint32_t pa = 0;             // parity of slot a's current use
-      int kb = 0, kin = 0, cb = 0;  // k-block in the tile / in the accumulation unit
-      uint32_t d_tmem = tmem_base;
-      for (int item = 0; item < total_items; ++item) {
-        if (kin == 0) {
-          cb = cc & 1;
-          if (!mbar_wait(acc_empty(cb), ((cc >> 1) & 1) ^ 1, abort_flag, p.status)) break;
-          d_tmem = tmem_base + (L::kPromote ? L::kChunkCols * (1 + cb) : BN * cb);
-        }
-        // the converters arrive on t_full only after they saw the stage's TMA
-        // (A and B) complete on s1_full and wrote its A operands
-        if (direct ? !mbar_wait(s1_full(s), (item / S1) & 1, abort_flag, p.status)
-                   : !mbar_wait(t_full(a), pa, abort_flag, p.status))
-          break;
-        tc_fence_after();
-        const uint32_t ahi = tmem_base + L::kACol0 + a * L::kAStageCols;  // 3xTF32: A hi | lo
-        const uint32_t alo = ahi + kBK;
-        const uint64_t da = smem_desc_sw128(a_raw + s * L::kARaw);  // TF32: A as landed
-        const uint64_t dbh = (L::kBf16 && !L::kABf16) ? smem_desc_sw64(b_hi + s * L::kBStride)
-                                                       : smem_desc_sw128(b_hi + s * L::kBStride);
-        uint64_t dbl = 0;
-        if constexpr (L::kSplit) dbl = smem_desc_sw128(b_lo + s * L::kBStride);
-        if constexpr (L::kABf16) {
+      int kb = 0;                  // k-block in the tile
+      // One accumulation unit (a chunk of kChunkKB k-blocks, or a whole tile
+      // when the accumulator is not promoted) per outer iteration; the inner
+      // loop is unrolled so that its k-blocks run without a loop back-edge or
+      // bookkeeping between them (those cost ~400 cycles of this thread's time
+      // per k-block, and this thread's issue rate bounds the kernel).
+      for (int item = 0; ok && item < total_items;) {
+        const int cb = cc & 1;
+        if (!mbar_wait(acc_empty(cb), ((cc >> 1) & 1) ^ 1, abort_flag, p.status)) break;
+        const uint32_t d_tmem = tmem_base + (L::kPromote ? L::kChunkCols * (1 + cb) : BN * cb);
+        const int len = L::kPromote ? min(L::kChunkKB, nkb - kb) : nkb - kb;
+        constexpr int kU = 4;  // k-blocks per unrolled group (kChunkKB when promoting)
+        static_assert(!L::kPromote || L::kChunkKB == kU, "one unrolled group per chunk");
+        for (int k0 = 0; ok && k0 < len; k0 += kU) {
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk)  // A and B from shared memory, 128-byte rows
-            tc_mma<1>(d_tmem, da + (uint64_t)(kk * 2), dbh + (uint64_t)(kk * 2), idesc_bf, (kin | kk) ? 1u : 0u);
-        } else if constexpr (L::kBf16) {
+        for (int u = 0; u < kU; ++u) {
+          const int kin = k0 + u;
+          if (kin >= len) break;
+          // the converters arrive on t_full only after they saw the stage's TMA
+          // (A and B) complete on s1_full and wrote its A operands
+          if (direct ? !mbar_wait(s1_full(s), (item / S1) & 1, abort_flag, p.status)
+                     : !mbar_wait(t_full(a), pa, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t ahi = tmem_base + L::kACol0 + a * L::kAStageCols;  // 3xTF32: A hi | lo
+          const uint32_t alo = ahi + kBK;
+          const uint64_t da = smem_desc_sw128(a_raw + s * L::kARaw);  // TF32: A as landed
+          const uint64_t dbh = (L::kBf16 && !L::kABf16) ? smem_desc_sw64(b_hi + s * L::kBStride)
+                                                         : smem_desc_sw128(b_hi + s * L::kBStride);
+          uint64_t dbl = 0;
+          if constexpr (L::kSplit) dbl = smem_desc_sw128(b_lo + s * L::kBStride);
+          if constexpr (L::kABf16) {
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk)  // K = 16 bf16 (32 bytes) per MMA
-            tc_mma_f16_ts(d_tmem, ahi + kk * 8, dbh + (uint64_t)(kk * 2), idesc_bf, (kin | kk) ? 1u : 0u);
-        }
+            for (int kk = 0; kk < kBK / 16; ++kk)  // A and B from shared memory, 128-byte rows
+              tc_mma<1>(d_tmem, da + (uint64_t)(kk * 2), dbh + (uint64_t)(kk * 2), idesc_bf, (kin | kk) ? 1u : 0u);
+          } else if constexpr (L::kBf16) {
 #pragma unroll
-        for (int kk = 0; kk < (L::kBf16 ? 0 : kBK / 8); ++kk) {
-          const uint32_t acc = (kin | kk) ? 1u : 0u;
-          if constexpr (L::kStack) {
-            // [hi.b_hi | hi.b_lo] over B hi and B lo rows, then lo.b_hi into the
-            // second (small-term) half
-            tc_mma_tf32_ts(d_tmem, ahi + kk * 8, dbh + (uint64_t)(kk * 2), idesc2, acc);
-            tc_mma_tf32_ts(d_tmem + BN, alo + kk * 8, dbh + (uint64_t)(kk * 2), idesc, 1u);
-          } else if constexpr (L::kSplit) {
-            tc_mma_tf32_ts(d_tmem, ahi + kk * 8, dbh + (uint64_t)(kk * 2), idesc, acc);
-            tc_mma_tf32_ts(d_tmem, ahi + kk * 8, dbl + (uint64_t)(kk * 2), idesc, 1u);
-            tc_mma_tf32_ts(d_tmem, alo + kk * 8, dbh + (uint64_t)(kk * 2), idesc, 1u);
-          } else {
-            tc_mma<0>(d_tmem, da + (uint64_t)(kk * 2), dbh + (uint64_t)(kk * 2), idesc, acc);
+            for (int kk = 0; kk < kBK / 16; ++kk)  // K = 16 bf16 (32 bytes) per MMA
+              tc_mma_f16_ts(d_tmem, ahi + kk * 8, dbh + (uint64_t)(kk * 2), idesc_bf, (kin | kk) ? 1u : 0u);
+          }
+#pragma unroll
+          for (int kk = 0; kk < (L::kBf16 ? 0 : kBK / 8); ++kk) {
+            const uint32_t acc = (kin | kk) ? 1u : 0u;
+            if constexpr (L::kStack) {
+              // [hi.b_hi | hi.b_lo] over B hi and B lo rows, then lo.b_hi into the
+              // second (small-term) half
+              tc_mma_tf32_ts(d_tmem, ahi + kk * 8, dbh + (uint64_t)(kk * 2), idesc2, acc);
+              tc_mma_tf32_ts(d_tmem + BN, alo + kk * 8, dbh + (uint64_t)(kk * 2), idesc, 1u);
+            } else if constexpr (L::kSplit) {
+              tc_mma_tf32_ts(d_tmem, ahi + kk * 8, dbh + (uint64_t)(kk * 2), idesc, acc);
+              tc_mma_tf32_ts(d_tmem, ahi + kk * 8, dbl + (uint64_t)(kk * 2), idesc, 1u);
+              tc_mma_tf32_ts(d_tmem, alo + kk * 8, dbh + (uint64_t)(kk * 2), idesc, 1u);
+            } else {
+              tc_mma<0>(d_tmem, da + (uint64_t)(kk * 2), dbh + (uint64_t)(kk * 2), idesc, acc);
+            }
+          }
+          // frees the shared-memory stage (and, through it, the TMEM A slot: the
+          // converters wait for this commit before refilling the slot)
+          tc_commit(s1_empty(s));
+          issued = true;
+          ++item;
+          if (++s == S1) s = 0;
+          if (++a == S2) {
+            a = 0;
+            pa ^= 1;
           }
         }
-        // frees the shared-memory stage (and, through it, the TMEM A slot: the
-        // converters wait for this commit before refilling the slot)
-        tc_commit(s1_empty(s));
-        issued = true;
-        const bool tile_end = ++kb == nkb;
-        if (tile_end) kb = 0;
-        if (tile_end || (L::kPromote && kin + 1 == L::kChunkKB)) {
-          tc_commit(acc_full(cb));
-          ++cc;
-          kin = 0;
-        } else {
-          ++kin;
         }
-        if (++s == S1) s = 0;
-        if (++a == S2) {
-          a = 0;
-          pa ^= 1;
-        }
+        if (!ok) break;
+        kb += len;
+        if (kb == nkb) kb = 0;
+        tc_commit(acc_full(cb));
+        ++cc;
       }
       // every MMA issued by this thread completes before TMEM is freed
       if (issued) {
