@@ -43,10 +43,11 @@ METRIC = "ResNet-50 v1.5 images/sec (batch 256, fp32 via 3xTF32)"
 METRIC_FAST = {"tf32": "ResNet-50 v1.5 images/sec (batch 256, fast mode: 1xTF32)",
                "bf16": "ResNet-50 v1.5 images/sec (batch 256, fast mode: BF16)",
                "fp32": "ResNet-50 v1.5 images/sec (batch 256, fp32 on CUDA cores)"}
-# DRAM bytes per igemm_tc3_kernel launch, mean over the 54 launches of one
-# batch-256 3xTF32 run: dram__bytes_read.sum + dram__bytes_write.sum from an
-# ncu DRAM capture of this workload (a measured constant, not re-derived here).
-TRAFFIC_PER_LAUNCH_3XTF32 = 467.5e6
+# DRAM bytes per igemm_tc3_kernel launch, mean over the 50 launches of one
+# batch-256 3xTF32 run (49 convolution steps and the classifier Gemm):
+# dram__bytes_read.sum + dram__bytes_write.sum from an ncu DRAM capture of this
+# workload (a measured constant, not re-derived here).
+TRAFFIC_PER_LAUNCH_3XTF32 = 446.8e6
 L2_BYTES = 126 * 1024 * 1024
 
 
