@@ -686,7 +686,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const bool last = ch == nch - 1;
         const uint32_t ccol = L::kPromote ? L::kChunkCols * (1 + cb) : cb * BN;  // accumulator columns
-        if (L::kStack && !last) {
+        // Promoted accumulators: every chunk, the tile's last one included, is
+        // folded into the running total and its accumulator handed back to the
+        // MMA thread at once; the output groups are then produced from the total,
+        // so the next tile's MMAs do not wait for this tile's stores.
+        if (L::kStack) {
           // total += big + small, 16 columns at a time
           for (int c = 0; c < BN; c += 16) {
             uint32_t a0[16], s0[16], b0[16];
@@ -702,7 +706,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             tmem_st_32x32b_x16(tmem_base + lane_addr + c, a0);
           }
-        } else if (L::kPromote && !last) {
+        } else if (L::kPromote) {
           // fold the chunk into the running total: each TMEM round trip carries
           // 32 columns of the chunk and 32 of the total (loads issued before
           // one wait), in 16-column pieces to bound live registers
@@ -727,27 +731,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_st_32x32b_x16(tmem_base + lane_addr + c + 16, a1);
           }
         }
+        if (L::kPromote) {
+          tmem_st_wait();  // the folded total is in TMEM
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(acc_empty(cb));
+        }
         for (int j = 0; j < ngroups && last; ++j) {
           uint32_t r[kEG];
-          tmem_ld_cols(tmem_base + lane_addr + ccol + j * kEG, r);
-          if constexpr (L::kStack) {  // big + small halves of the chunk
-            uint32_t sm[kEG];
-            tmem_ld_cols(tmem_base + lane_addr + ccol + BN + j * kEG, sm);
-            tmem_ld_wait();
-#pragma unroll
-            for (int e = 0; e < kEG; ++e)
-              r[e] = __float_as_uint(__uint_as_float(r[e]) + __uint_as_float(sm[e]));
-          }
-          if (L::kPromote && ch > 0) {
-            uint32_t t[kEG];
-            tmem_ld_cols(tmem_base + lane_addr + j * kEG, t);
-            tmem_ld_wait();
-#pragma unroll
-            for (int e = 0; e < kEG; ++e)
-              r[e] = __float_as_uint(__uint_as_float(t[e]) + __uint_as_float(r[e]));
-          } else {
-            tmem_ld_wait();
-          }
+          // the running total (promoted) or the tile's accumulator
+          tmem_ld_cols(tmem_base + lane_addr + (L::kPromote ? 0u : ccol) + j * kEG, r);
+          tmem_ld_wait();
           // ---- final values of this group
           const int col0 = nt * BN + j * kEG;
           const int buf = grp % NB;
@@ -819,10 +813,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           ++grp;
         }
-        if (!last) tmem_st_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(acc_empty(cb));
+        if (!L::kPromote) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(acc_empty(cb));
+        }
         if (L::kPromote) ++cc;
       }
     }
