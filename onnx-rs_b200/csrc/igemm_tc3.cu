@@ -737,81 +737,107 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(acc_empty(cb));
         }
-        for (int j = 0; j < ngroups && last; ++j) {
-          uint32_t r[kEG];
-          // the running total (promoted) or the tile's accumulator
-          tmem_ld_cols(tmem_base + lane_addr + (L::kPromote ? 0u : ccol) + j * kEG, r);
-          tmem_ld_wait();
+        // one output group: the running total (promoted) or the tile's
+        // accumulator, columns [j * kEG, (j + 1) * kEG), in registers r
+        const uint32_t gcol = L::kPromote ? 0u : ccol;
+        auto out_group = [&](int j, const uint32_t (&r)[kEG]) -> bool {
           // ---- final values of this group
-          const int col0 = nt * BN + j * kEG;
-          const int buf = grp % NB;
-          float v[kEG];
+            const int col0 = nt * BN + j * kEG;
+            const int buf = grp % NB;
+            float v[kEG];
 #pragma unroll
-          for (int e = 0; e < kEG; ++e) v[e] = __uint_as_float(r[e]);
+            for (int e = 0; e < kEG; ++e) v[e] = __uint_as_float(r[e]);
 #pragma unroll
-          for (int q4 = 0; q4 < kEG / 4; ++q4) {
-            const int c = j * kEG + 4 * q4;  // column within the tile
-            if (p.scale) {
-              const float4 sc = *reinterpret_cast<const float4*>(ss_scale + c);
-              v[4 * q4] *= sc.x; v[4 * q4 + 1] *= sc.y; v[4 * q4 + 2] *= sc.z; v[4 * q4 + 3] *= sc.w;
+            for (int q4 = 0; q4 < kEG / 4; ++q4) {
+              const int c = j * kEG + 4 * q4;  // column within the tile
+              if (p.scale) {
+                const float4 sc = *reinterpret_cast<const float4*>(ss_scale + c);
+                v[4 * q4] *= sc.x; v[4 * q4 + 1] *= sc.y; v[4 * q4 + 2] *= sc.z; v[4 * q4 + 3] *= sc.w;
+              }
+              if (p.shift) {
+                const float4 sh = *reinterpret_cast<const float4*>(ss_shift + c);
+                v[4 * q4] += sh.x; v[4 * q4 + 1] += sh.y; v[4 * q4 + 2] += sh.z; v[4 * q4 + 3] += sh.w;
+              }
             }
-            if (p.shift) {
-              const float4 sh = *reinterpret_cast<const float4*>(ss_shift + c);
-              v[4 * q4] += sh.x; v[4 * q4 + 1] += sh.y; v[4 * q4 + 2] += sh.z; v[4 * q4 + 3] += sh.w;
+            bool w = true;
+            if (p.res && rows_in) {
+              w = mbar_wait(res_full(warp, buf), (grp / NB) & 1, abort_flag, p.status);
+              if (w && lane == 0) res_out &= ~(1u << buf);
+              if constexpr (L::kOBf16) {
+#pragma unroll
+                for (int q8 = 0; q8 < kEG / 8; ++q8) {
+                  const uint4 rv = lds_u4(res_st + buf * kEpiTile + swz_eg<L::kEpiRow>(et, q8));
+                  v[8 * q8] += bf16_lo(rv.x); v[8 * q8 + 1] += bf16_hi(rv.x);
+                  v[8 * q8 + 2] += bf16_lo(rv.y); v[8 * q8 + 3] += bf16_hi(rv.y);
+                  v[8 * q8 + 4] += bf16_lo(rv.z); v[8 * q8 + 5] += bf16_hi(rv.z);
+                  v[8 * q8 + 6] += bf16_lo(rv.w); v[8 * q8 + 7] += bf16_hi(rv.w);
+                }
+              } else {
+#pragma unroll
+                for (int q4 = 0; q4 < kEG / 4; ++q4) {
+                  const float4 rv = ld_shared_f4(res_st + buf * kEpiTile + swz_eg<L::kEpiRow>(et, q4));
+                  v[4 * q4] += rv.x; v[4 * q4 + 1] += rv.y; v[4 * q4 + 2] += rv.z; v[4 * q4 + 3] += rv.w;
+                }
+              }
             }
-          }
-          bool w = true;
-          if (p.res && rows_in) {
-            w = mbar_wait(res_full(warp, buf), (grp / NB) & 1, abort_flag, p.status);
-            if (w && lane == 0) res_out &= ~(1u << buf);
+            if (p.relu) {
+#pragma unroll
+              for (int e = 0; e < kEG; ++e) v[e] = v[e] > 0.f ? v[e] : 0.f;
+            }
+            // this warp's staging rows of NB groups ago must have been read by its
+            // TMA store (the warp vote below also orders lane 0's wait first)
+            if (lane == 0) bulk_wait_group_read<NB - 1>();
+            if (!__all_sync(0xffffffffu, w)) {
+              return false;  // decided with the other warps at the next barrier
+            }
+            const uint32_t ost = out_st + buf * kEpiTile;
             if constexpr (L::kOBf16) {
 #pragma unroll
-              for (int q8 = 0; q8 < kEG / 8; ++q8) {
-                const uint4 rv = lds_u4(res_st + buf * kEpiTile + swz_eg<L::kEpiRow>(et, q8));
-                v[8 * q8] += bf16_lo(rv.x); v[8 * q8 + 1] += bf16_hi(rv.x);
-                v[8 * q8 + 2] += bf16_lo(rv.y); v[8 * q8 + 3] += bf16_hi(rv.y);
-                v[8 * q8 + 4] += bf16_lo(rv.z); v[8 * q8 + 5] += bf16_hi(rv.z);
-                v[8 * q8 + 6] += bf16_lo(rv.w); v[8 * q8 + 7] += bf16_hi(rv.w);
-              }
+              for (int q8 = 0; q8 < kEG / 8; ++q8)
+                sts_u4(ost + swz_eg<L::kEpiRow>(et, q8), pack_bf16x2(v[8 * q8], v[8 * q8 + 1]),
+                       pack_bf16x2(v[8 * q8 + 2], v[8 * q8 + 3]), pack_bf16x2(v[8 * q8 + 4], v[8 * q8 + 5]),
+                       pack_bf16x2(v[8 * q8 + 6], v[8 * q8 + 7]));
             } else {
 #pragma unroll
-              for (int q4 = 0; q4 < kEG / 4; ++q4) {
-                const float4 rv = ld_shared_f4(res_st + buf * kEpiTile + swz_eg<L::kEpiRow>(et, q4));
-                v[4 * q4] += rv.x; v[4 * q4 + 1] += rv.y; v[4 * q4 + 2] += rv.z; v[4 * q4 + 3] += rv.w;
-              }
+              for (int q4 = 0; q4 < kEG / 4; ++q4)
+                sts_v4(ost + swz_eg<L::kEpiRow>(et, q4), v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
             }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0 && rows_in) {
+              tma_store_3d(&tm_y, col0, r0, b, ost + warp * kWTile);
+              bulk_commit_group();
+              if (p.res && j + NB < ngroups) issue_res(grp + NB, col0 + NB * kEG, r0, b);  // freed buffer
+            }
+            ++grp;
+            return true;
+        };
+        if (kEG > 16 && last) {
+          // 32-column groups: one TMEM round trip per group (two groups' worth of
+          // registers would spill at the 128 registers a 416-thread block gets)
+          for (int j = 0; j < ngroups; ++j) {
+            uint32_t r[kEG];
+            tmem_ld_cols(tmem_base + lane_addr + gcol + j * kEG, r);
+            tmem_ld_wait();
+            if (!out_group(j, r)) { ok = false; break; }
           }
-          if (p.relu) {
-#pragma unroll
-            for (int e = 0; e < kEG; ++e) v[e] = v[e] > 0.f ? v[e] : 0.f;
+        } else if (last && ngroups > 0) {
+          // the TMEM load of group j + 1 is in flight while group j is scaled,
+          // staged and stored
+          uint32_t ra[kEG], rb[kEG];
+          tmem_ld_cols(tmem_base + lane_addr + gcol, ra);
+          tmem_ld_wait();
+          for (int j = 0; j < ngroups; j += 2) {
+            if (j + 1 < ngroups) tmem_ld_cols(tmem_base + lane_addr + gcol + (j + 1) * kEG, rb);
+            const bool g_ok = out_group(j, ra);
+            tmem_ld_wait();
+            if (!g_ok) { ok = false; break; }
+            if (j + 1 >= ngroups) break;
+            if (j + 2 < ngroups) tmem_ld_cols(tmem_base + lane_addr + gcol + (j + 2) * kEG, ra);
+            const bool g_ok2 = out_group(j + 1, rb);
+            tmem_ld_wait();
+            if (!g_ok2) { ok = false; break; }
           }
-          // this warp's staging rows of NB groups ago must have been read by its
-          // TMA store (the warp vote below also orders lane 0's wait first)
-          if (lane == 0) bulk_wait_group_read<NB - 1>();
-          if (!__all_sync(0xffffffffu, w)) {
-            ok = false;  // decided with the other warps at the next barrier
-            break;
-          }
-          const uint32_t ost = out_st + buf * kEpiTile;
-          if constexpr (L::kOBf16) {
-#pragma unroll
-            for (int q8 = 0; q8 < kEG / 8; ++q8)
-              sts_u4(ost + swz_eg<L::kEpiRow>(et, q8), pack_bf16x2(v[8 * q8], v[8 * q8 + 1]),
-                     pack_bf16x2(v[8 * q8 + 2], v[8 * q8 + 3]), pack_bf16x2(v[8 * q8 + 4], v[8 * q8 + 5]),
-                     pack_bf16x2(v[8 * q8 + 6], v[8 * q8 + 7]));
-          } else {
-#pragma unroll
-            for (int q4 = 0; q4 < kEG / 4; ++q4)
-              sts_v4(ost + swz_eg<L::kEpiRow>(et, q4), v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
-          }
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0 && rows_in) {
-            tma_store_3d(&tm_y, col0, r0, b, ost + warp * kWTile);
-            bulk_commit_group();
-            if (p.res && j + NB < ngroups) issue_res(grp + NB, col0 + NB * kEG, r0, b);  // freed buffer
-          }
-          ++grp;
         }
         if (!L::kPromote) {
           tc_fence_before();
