@@ -692,6 +692,53 @@ __global__ void maxpool_nhwc_v4_kernel(const float* __restrict__ x, int N, int C
   }
 }
 
+// 3x3 stride-2 MaxPool (the ResNet stem's) over output-row segments: a thread
+// takes P consecutive outputs of one row for 4 channels and loads each input
+// vector of the segment's three input rows once (2P+1 per row where per-output
+// threads load 3P).  Per output the maxima are taken in the same order as
+// maxpool_nhwc_v4_kernel (rows, then columns), so the results are identical.
+template <int P>
+__global__ void maxpool3s2_nhwc_v4_kernel(const float4* __restrict__ x, int C4, int Cs4, int H, int W,
+                                          int pt, int pl, int OH, int OW, int nseg, unsigned total,
+                                          float4* __restrict__ y) {
+  for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const int c4 = (int)(i % (unsigned)C4);
+    unsigned t = i / (unsigned)C4;
+    const int seg = (int)(t % (unsigned)nseg);
+    t /= (unsigned)nseg;
+    const int oh = (int)(t % (unsigned)OH);
+    const unsigned n = t / (unsigned)OH;
+    const int ow0 = seg * P, iw0 = 2 * ow0 - pl;
+    float4 m[P];
+#pragma unroll
+    for (int q = 0; q < P; ++q)
+      m[q] = make_float4(-3.40282347e+38f, -3.40282347e+38f, -3.40282347e+38f, -3.40282347e+38f);
+    for (int r = 0; r < 3; ++r) {
+      const int ih = 2 * oh - pt + r;
+      if ((unsigned)ih >= (unsigned)H) continue;
+      const float4* row = x + ((size_t)n * H + ih) * W * Cs4 + c4;
+#pragma unroll
+      for (int j = 0; j < 2 * P + 1; ++j) {
+        const int iw = iw0 + j;
+        if ((unsigned)iw >= (unsigned)W) continue;
+        const float4 v = __ldg(row + (size_t)iw * Cs4);
+#pragma unroll
+        for (int q = 0; q < P; ++q)
+          if (j >= 2 * q && j <= 2 * q + 2) {
+            m[q].x = fmaxf(m[q].x, v.x);
+            m[q].y = fmaxf(m[q].y, v.y);
+            m[q].z = fmaxf(m[q].z, v.z);
+            m[q].w = fmaxf(m[q].w, v.w);
+          }
+      }
+    }
+    float4* yo = y + (((size_t)n * OH + oh) * OW + ow0) * Cs4 + c4;
+#pragma unroll
+    for (int q = 0; q < P; ++q)
+      if (ow0 + q < OW) yo[(size_t)q * Cs4] = m[q];
+  }
+}
+
 // Scalar path with indices: the ONNX flat NCHW index of the first maximum.
 __global__ void maxpool_nhwc_idx_kernel(const float* __restrict__ x, int N, int C, int Cs, int H,
                                         int W, int KH, int KW, int sh, int sw, int pt, int pl,
@@ -729,6 +776,18 @@ int maxpool_nhwc_launch(const float* x, int N, int C, int Cs, int H, int W, int 
                         int sw, int pt, int pl, int OH, int OW, float* y, long long* ind,
                         cudaStream_t st) {
   const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15) == 0;
+  if (!ind && C % 4 == 0 && Cs % 4 == 0 && aligned && KH == 3 && KW == 3 && sh == 2 && sw == 2) {
+    constexpr int kP = 8;  // outputs per thread
+    const int nseg = (OW + kP - 1) / kP;
+    const long long total = (long long)N * OH * nseg * (C / 4);
+    if (total == 0) return 0;
+    if (total < (1ll << 31)) {
+      maxpool3s2_nhwc_v4_kernel<kP><<<grid_for(total, kBlock), kBlock, 0, st>>>(
+          reinterpret_cast<const float4*>(x), C / 4, Cs / 4, H, W, pt, pl, OH, OW, nseg, (unsigned)total,
+          reinterpret_cast<float4*>(y));
+      return (int)cudaGetLastError();
+    }
+  }
   if (!ind && C % 4 == 0 && Cs % 4 == 0 && aligned) {
     const long long total = (long long)N * OH * OW * (C / 4);
     if (total == 0) return 0;

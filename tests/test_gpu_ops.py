@@ -304,6 +304,15 @@ def test_maxpool_and_indices(ob, oracle, ctx):
     ref, rind = oracle.maxpool2d(x, (2, 3), (2, 2), (0, 1, 1, 0), ceil_mode=1, with_indices=True)
     np.testing.assert_array_equal(np_(y), ref)
     np.testing.assert_array_equal(np_(ind), rind)
+    # 3x3 stride 2 without indices (row-segment kernel): output rows that end
+    # mid-segment, asymmetric pads, ceil mode, NaN and -inf inputs
+    x = rng.standard_normal((3, 12, 15, 37)).astype(np.float32)
+    x[1, 4, 3, 5] = np.nan
+    x[2, 7, :, 9] = -np.inf
+    for pads, ceil in (((1, 0, 0, 1), 1), ((0, 1, 1, 1), 0), ((1, 1, 1, 1), 0)):
+        y = ob.MaxPool((3, 3), (2, 2), pads, ceil_mode=ceil).compute([cu(x)], ctx)[0]
+        ref = oracle.maxpool2d(x, (3, 3), (2, 2), pads, ceil_mode=ceil)
+        np.testing.assert_array_equal(np_(y), ref)
 
 
 def test_gap_relu_add_bn(ob, oracle, ctx):
