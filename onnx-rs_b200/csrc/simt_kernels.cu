@@ -695,7 +695,8 @@ __global__ void maxpool_nhwc_v4_kernel(const float* __restrict__ x, int N, int C
 // 3x3 stride-2 MaxPool (the ResNet stem's) over output-row segments: a thread
 // takes P consecutive outputs of one row for 4 channels and loads each input
 // vector of the segment's three input rows once (2P+1 per row where per-output
-// threads load 3P).  Per output the maxima are taken in the same order as
+// threads load 3P; longer segments lose more to fewer threads in flight than
+// they save in loads).  Per output the maxima are taken in the same order as
 // maxpool_nhwc_v4_kernel (rows, then columns), so the results are identical.
 template <int P>
 __global__ void maxpool3s2_nhwc_v4_kernel(const float4* __restrict__ x, int C4, int Cs4, int H, int W,
@@ -777,7 +778,7 @@ int maxpool_nhwc_launch(const float* x, int N, int C, int Cs, int H, int W, int 
                         cudaStream_t st) {
   const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15) == 0;
   if (!ind && C % 4 == 0 && Cs % 4 == 0 && aligned && KH == 3 && KW == 3 && sh == 2 && sw == 2) {
-    constexpr int kP = 8;  // outputs per thread
+    constexpr int kP = 2;  // outputs per thread (1 / 2 / 4 / 8: 0.236 / 0.224 / 0.303 / 0.525 ms at batch 256)
     const int nseg = (OW + kP - 1) / kP;
     const long long total = (long long)N * OH * nseg * (C / 4);
     if (total == 0) return 0;
