@@ -174,9 +174,9 @@ static void choose_tiling(onnxb200_handle* h, onnxb200_conv_plan* p, bool residu
   q.batches = 1;
   q.num_kb = p->num_kb;
   q.a_bf16 = p->a_bf16;
-  q.res = residual ? reinterpret_cast<const float*>(p) : nullptr;  // a flag here, never read
+  q.out_bf16 = p->out_bf16;
   int bn = 128, ks = 1;
-  igemm_pick_split(q, p->prec, h->num_sms, &bn, &ks);
+  igemm_pick_split(q, residual, p->prec, h->num_sms, &bn, &ks);
   p->bn = bn;
   p->ksplit = ks;
   p->split_bytes = ks > 1 ? (size_t)ks * q.M * q.Nc * sizeof(float) : 0;
@@ -550,7 +550,7 @@ int gemm_tc_run(onnxb200_handle* h, const GemmCall& c, const void* b_hi, const v
   int bn = igemm_pick_bn(q, prec, h->num_sms), ks = 1;
   if (c.split_ws) {
     int b2 = bn, k2 = 1;
-    igemm_pick_split(q, prec, h->num_sms, &b2, &k2);
+    igemm_pick_split(q, q.res != nullptr, prec, h->num_sms, &b2, &k2);
     if (k2 > 1 && (size_t)k2 * q.M * q.Nc * sizeof(float) <= c.split_bytes) {
       bn = b2;
       ks = k2;
@@ -582,9 +582,8 @@ size_t gemm_split_bytes(const onnxb200_handle* h, int M, int N, int kpad, int pr
   q.Nc = N;
   q.batches = 1;
   q.num_kb = kpad / igemm_block_k(prec);
-  q.res = residual ? reinterpret_cast<const float*>(h) : nullptr;  // a flag here, never read
   int bn = 128, ks = 1;
-  igemm_pick_split(q, prec, h->num_sms, &bn, &ks);
+  igemm_pick_split(q, residual, prec, h->num_sms, &bn, &ks);
   return ks > 1 ? (size_t)ks * M * N * sizeof(float) : 0;
 }
 

@@ -24,10 +24,14 @@ int igemm_pick_bn(const IgemmParams& p, int precision, int num_sms) {
   // when twice as many tiles still fit in one wave, so that more SMs work.
   const long long mt = (long long)((p.M + kBM - 1) / kBM) * p.batches;
   if (2 * mt * ((nc + 127) / 128) <= num_sms) return 64;
-  // 3xTF32 (chunked accumulators, 3 x BN columns) and BF16 keep A slots in TMEM
-  // next to the accumulators: at most 128 columns wide.  TF32 keeps only two
-  // whole-tile accumulators, so 256 fits the 512 TMEM columns.
-  if (precision == kPrec3xTF32 || precision == kPrecBF16) return 128;
+  // 3xTF32 (chunked accumulators, 3 x BN columns) and BF16 from fp32 activations
+  // keep A slots in TMEM next to the accumulators: at most 128 columns wide.
+  // TF32 and BF16 with bf16 activations and outputs keep only two whole-tile
+  // accumulators, so 256 fits the 512 TMEM columns: twice the work per MMA
+  // instruction (one thread issues them all) when there are enough tiles.
+  const bool wide_ok = precision == kPrecTF32 || (precision == kPrecBF16 && p.a_bf16 && p.out_bf16 &&
+                                                  p.num_kb > 2);
+  if (!wide_ok) return 128;
   // Wide tiles halve A re-reads; use them when there are enough tiles to fill the GPU.
   if (nc >= 256 && mt * ((nc + 255) / 256) >= 2ll * num_sms) return 256;
   return 128;
@@ -109,7 +113,7 @@ int igemm_launch_split(const IgemmParams& p, int ksplit, float* ws, const CUtens
                               p.out_bf16, st);
 }
 
-void igemm_pick_split(const IgemmParams& p, int precision, int num_sms, int* bn, int* ksplit) {
+void igemm_pick_split(const IgemmParams& p, bool residual, int precision, int num_sms, int* bn, int* ksplit) {
   const int bn0 = igemm_pick_bn(p, precision, num_sms);
   *bn = bn0;
   *ksplit = 1;
@@ -127,7 +131,7 @@ void igemm_pick_split(const IgemmParams& p, int precision, int num_sms, int* bn,
                   // ~10 TB/s), read the residual and write y from / to HBM (~6 TB/s)
       const double slice = (double)p.M * p.Nc * 4.0;
       const double ws_gbs = s * slice <= 64e6 ? 10.0e6 : 6.0e6;  // bytes per us
-      c += (s * slice / ws_gbs + (1 + (p.res ? 1 : 0)) * slice / 6.0e6 + 2.0) / kb_us;
+      c += (s * slice / ws_gbs + (1 + (residual ? 1 : 0)) * slice / 6.0e6 + 2.0) / kb_us;
     }
     return c;
   };

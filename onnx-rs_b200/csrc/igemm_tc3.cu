@@ -85,7 +85,8 @@ struct Layout {
   static constexpr int kBBytes = BN * kBK * (kBf16 ? 2 : 4);  // one B operand (hi or lo)
   static constexpr int kStage = kARaw + (kSplit ? 2 : 1) * kBBytes;
   static constexpr int kEpiBytes = 2 * NB * kEpiTile;  // out[NB] + res[NB]
-  static constexpr int kS1raw = (kSmemBudget - kEpiBytes) / kStage;
+  // (256-column tiles also leave room for their 2 KB of staged scale / shift)
+  static constexpr int kS1raw = (kSmemBudget - kEpiBytes - (BN > 128 ? 2 * BN * 4 : 0)) / kStage;
   static constexpr int kS1cap = kS1raw > 8 ? 8 : kS1raw;
   static constexpr bool kPromote = kSplit;
   static constexpr int kChunkKB = kPromote ? 4 : (1 << 30);  // 48 MMAs per chunk
@@ -973,6 +974,7 @@ int igemm3_launch(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap
   // bf16 activations (AIO bit 0) and / or bf16 outputs (bit 1)
   const int aio = (p.a_bf16 ? 1 : 0) | (p.out_bf16 ? 2 : 0);
   if (aio && precision != kPrecBF16) return (int)cudaErrorInvalidValue;
+  if (aio == 3 && bn == 256 && !short_k) return launch3_t<kPrecBF16, 256, 32, 2, 3>(p, hi, lo, am, am2, num_sms, st);
   if (aio == 3 && bn == 64)
     return short_k ? launch3_t<kPrecBF16, 64, 32, 4, 3>(p, hi, lo, am, am2, num_sms, st)
                    : launch3_t<kPrecBF16, 64, 32, 2, 3>(p, hi, lo, am, am2, num_sms, st);

@@ -105,10 +105,11 @@ int igemm_launch_split(const IgemmParams& p, int ksplit, float* ws, const CUtens
                        const CUtensorMap& tm_lo, const CUtensorMap& tm_a, const CUtensorMap& tm_a2,
                        int precision, int bn, int num_sms, cudaStream_t stream);
 
-// Tile width and K split for a problem: igemm_pick_bn's width, or (when a K
-// split is modelled to be >= 10% faster: few output tiles, long K) the split
-// and the width to use with it.  *ksplit = 1 means no split.
-void igemm_pick_split(const IgemmParams& p, int precision, int num_sms, int* bn, int* ksplit);
+// Tile width and K split for a problem (geometry in p; `residual`: the epilogue
+// adds a residual): igemm_pick_bn's width, or (when a K split is modelled to be
+// >= 10% faster: few output tiles, long K) the split and the width to use with
+// it.  *ksplit = 1 means no split.
+void igemm_pick_split(const IgemmParams& p, bool residual, int precision, int num_sms, int* bn, int* ksplit);
 
 // Sums ksplit slices of [M][N] fp32 partial sums (slice order) and applies the
 // epilogue: y = relu(sum * scale + shift + res); y / res are bf16 when out_bf16.
