@@ -89,7 +89,10 @@ struct Layout {
   static constexpr int kS1raw = (kSmemBudget - kEpiBytes - (BN > 128 ? 2 * BN * 4 : 0)) / kStage;
   static constexpr int kS1cap = kS1raw > 8 ? 8 : kS1raw;
   static constexpr bool kPromote = kSplit;
-  static constexpr int kChunkKB = kPromote ? 4 : (1 << 30);  // 48 MMAs per chunk
+  // k-blocks per TMEM accumulator chunk.  With BN = 64 (stacked B, below) the
+  // big-term half of the chunk takes only the a_hi.b_hi products: 8 k-blocks give
+  // it 32 truncating adds, fewer than the 48 of a 4-k-block three-product chunk.
+  static constexpr int kChunkKB = kPromote ? (BN == 64 ? 8 : 4) : (1 << 30);
   // 3xTF32 with BN = 64: B hi and B lo sit back to back in each stage, so one
   // N = 128 MMA computes [a_hi.b_hi | a_hi.b_lo] and an N = 64 MMA adds a_lo.b_hi
   // to the second half: two MMA instructions per K step instead of three (the
@@ -558,8 +561,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(acc_empty(cb), ((cc >> 1) & 1) ^ 1, abort_flag, p.status)) break;
         const uint32_t d_tmem = tmem_base + (L::kPromote ? L::kChunkCols * (1 + cb) : BN * cb);
         const int len = L::kPromote ? min(L::kChunkKB, nkb - kb) : nkb - kb;
-        constexpr int kU = 4;  // k-blocks per unrolled group (kChunkKB when promoting)
-        static_assert(!L::kPromote || L::kChunkKB == kU, "one unrolled group per chunk");
+        constexpr int kU = 4;  // k-blocks per unrolled group
+        static_assert(!L::kPromote || L::kChunkKB % kU == 0, "whole unrolled groups per chunk");
         for (int k0 = 0; ok && k0 < len; k0 += kU) {
 #pragma unroll
         for (int u = 0; u < kU; ++u) {
