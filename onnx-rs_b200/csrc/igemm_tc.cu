@@ -95,7 +95,7 @@ int igemm_launch_split(const IgemmParams& p, int ksplit, float* ws, const CUtens
                        int bn, int num_sms, cudaStream_t st) {
   if (ksplit <= 1) return igemm_launch(p, hi, lo, am, am2, precision, bn, num_sms, st);
   if (!ws || (reinterpret_cast<uintptr_t>(ws) & 15) || p.batches != 1 || p.a_off || p.b_row || p.a_bf16 ||
-      p.num_kb % ksplit)
+      p.out_bf16 || p.num_kb % ksplit)
     return (int)cudaErrorInvalidValue;
   // slice b's raw sums -> ws[b][M][Nc]
   IgemmParams q = p;
@@ -109,15 +109,14 @@ int igemm_launch_split(const IgemmParams& p, int ksplit, float* ws, const CUtens
   q.out_bf16 = 0;
   int rc = igemm_launch(q, hi, lo, am, am2, precision, bn, num_sms, st);
   if (rc) return rc;
-  return splitk_reduce_launch(ws, ksplit, p.M, p.Nc, p.y, p.ldy, p.scale, p.shift, p.res, p.ldr, p.relu,
-                              p.out_bf16, st);
+  return splitk_reduce_launch(ws, ksplit, p.M, p.Nc, p.y, p.ldy, p.scale, p.shift, p.res, p.ldr, p.relu, st);
 }
 
 void igemm_pick_split(const IgemmParams& p, bool residual, int precision, int num_sms, int* bn, int* ksplit) {
   const int bn0 = igemm_pick_bn(p, precision, num_sms);
   *bn = bn0;
   *ksplit = 1;
-  if (p.batches != 1 || p.a_off || p.b_row || p.a_bf16 || p.num_kb < 8 || num_sms <= 0) return;
+  if (p.batches != 1 || p.a_off || p.b_row || p.a_bf16 || p.out_bf16 || p.num_kb < 8 || num_sms <= 0) return;
   // modelled time in units of one k-block of a 128-column tile; a 64-column
   // tile's k-block costs ~0.8 of it (its MMAs are half as long, the operand
   // round trip is not)

@@ -99,8 +99,8 @@ int igemm3_launch(const IgemmParams& p, const CUtensorMap& tm_hi, const CUtensor
 // slices CTAs' worth of work, for problems with too few tiles to fill the GPU),
 // each slice storing raw fp32 partial sums to ws ([ksplit][M][Nc], 16-byte
 // aligned), then one reduction pass sums the slices in order and applies p's
-// epilogue (scale, shift, residual, Relu, bf16 output) into p.y.  ksplit <= 1 is
-// a plain igemm_launch.  Single-batch problems with fp32 activations only.
+// epilogue (scale, shift, residual, Relu) into p.y.  ksplit <= 1 is a plain
+// igemm_launch.  Single-batch problems with fp32 activations and outputs only.
 int igemm_launch_split(const IgemmParams& p, int ksplit, float* ws, const CUtensorMap& tm_hi,
                        const CUtensorMap& tm_lo, const CUtensorMap& tm_a, const CUtensorMap& tm_a2,
                        int precision, int bn, int num_sms, cudaStream_t stream);
@@ -108,14 +108,13 @@ int igemm_launch_split(const IgemmParams& p, int ksplit, float* ws, const CUtens
 // Tile width and K split for a problem (geometry in p; `residual`: the epilogue
 // adds a residual): igemm_pick_bn's width, or (when a K split is modelled to be
 // >= 10% faster: few output tiles, long K) the split and the width to use with
-// it.  *ksplit = 1 means no split.
+// it.  *ksplit = 1 means no split.  Only fp32 activations and outputs split.
 void igemm_pick_split(const IgemmParams& p, bool residual, int precision, int num_sms, int* bn, int* ksplit);
 
 // Sums ksplit slices of [M][N] fp32 partial sums (slice order) and applies the
-// epilogue: y = relu(sum * scale + shift + res); y / res are bf16 when out_bf16.
-int splitk_reduce_launch(const float* ws, int ksplit, int M, int N, void* y, int ldy, const float* scale,
-                         const float* shift, const void* res, int ldr, int relu, int out_bf16,
-                         cudaStream_t stream);
+// epilogue: y = relu(sum * scale + shift + res), all fp32.
+int splitk_reduce_launch(const float* ws, int ksplit, int M, int N, float* y, int ldy, const float* scale,
+                         const float* shift, const float* res, int ldr, int relu, cudaStream_t stream);
 
 // K elements per k-block of the kernel used for a precision (p.num_kb = Kpad / this):
 // 32, or 64 when the activations are stored as bf16 (128-byte rows either way).

@@ -286,9 +286,9 @@ int grouped_row_slice(int CO, int cg) {
 // y[m][n] = relu(sum_s ws[s][m][n] * scale[n] + shift[n] + res[m][n]), slices
 // summed in order; one thread per 4 consecutive columns (16-byte vectors).
 __global__ void splitk_reduce_kernel(const float4* __restrict__ ws, int S, long long MN4, int N4,
-                                     void* __restrict__ y, int ldy, const float* __restrict__ scale,
-                                     const float* __restrict__ shift, const void* __restrict__ res, int ldr,
-                                     int relu, int out_bf16) {
+                                     float* __restrict__ y, int ldy, const float* __restrict__ scale,
+                                     const float* __restrict__ shift, const float* __restrict__ res, int ldr,
+                                     int relu) {
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < MN4;
        i += (long long)gridDim.x * blockDim.x) {
     const long long m = i / N4;
@@ -307,43 +307,25 @@ __global__ void splitk_reduce_kernel(const float4* __restrict__ ws, int S, long 
       a.x += sh.x, a.y += sh.y, a.z += sh.z, a.w += sh.w;
     }
     if (res) {
-      const long long ro = m * ldr + n;
-      if (out_bf16) {
-        const uint2 rv = __ldg(reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(res) + ro));
-        a.x += __uint_as_float(rv.x << 16), a.y += __uint_as_float(rv.x & 0xffff0000u);
-        a.z += __uint_as_float(rv.y << 16), a.w += __uint_as_float(rv.y & 0xffff0000u);
-      } else {
-        const float4 rv = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(res) + ro));
-        a.x += rv.x, a.y += rv.y, a.z += rv.z, a.w += rv.w;
-      }
+      const float4 rv = __ldg(reinterpret_cast<const float4*>(res + m * ldr + n));
+      a.x += rv.x, a.y += rv.y, a.z += rv.z, a.w += rv.w;
     }
     if (relu) a = make_float4(fmaxf(a.x, 0.f), fmaxf(a.y, 0.f), fmaxf(a.z, 0.f), fmaxf(a.w, 0.f));
-    const long long yo = m * ldy + n;
-    if (out_bf16) {
-      const __nv_bfloat162 lo = __floats2bfloat162_rn(a.x, a.y), hi = __floats2bfloat162_rn(a.z, a.w);
-      uint2 v;
-      v.x = *reinterpret_cast<const uint32_t*>(&lo);
-      v.y = *reinterpret_cast<const uint32_t*>(&hi);
-      *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(y) + yo) = v;
-    } else {
-      *reinterpret_cast<float4*>(static_cast<float*>(y) + yo) = a;
-    }
+    *reinterpret_cast<float4*>(y + m * ldy + n) = a;
   }
 }
 
-int splitk_reduce_launch(const float* ws, int ksplit, int M, int N, void* y, int ldy, const float* scale,
-                         const float* shift, const void* res, int ldr, int relu, int out_bf16,
-                         cudaStream_t st) {
+int splitk_reduce_launch(const float* ws, int ksplit, int M, int N, float* y, int ldy, const float* scale,
+                         const float* shift, const float* res, int ldr, int relu, cudaStream_t st) {
   auto mis = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) != 0; };
-  if (ksplit < 1 || N % 4 || ldy % 4 || (res && ldr % 4) || !ws || !y || mis(ws) ||
-      (!out_bf16 && mis(y)) || (reinterpret_cast<uintptr_t>(y) & 7) || (scale && mis(scale)) ||
-      (shift && mis(shift)) || (res && (reinterpret_cast<uintptr_t>(res) & (out_bf16 ? 7 : 15))))
+  if (ksplit < 1 || N % 4 || ldy % 4 || (res && ldr % 4) || !ws || !y || mis(ws) || mis(y) ||
+      (scale && mis(scale)) || (shift && mis(shift)) || (res && mis(res)))
     return (int)cudaErrorMisalignedAddress;
   const long long mn4 = (long long)M * N / 4;
   if (mn4 == 0) return 0;
   const int blocks = (int)std::min<long long>((mn4 + kBlock - 1) / kBlock, 148LL * 16);
   splitk_reduce_kernel<<<blocks, kBlock, 0, st>>>(reinterpret_cast<const float4*>(ws), ksplit, mn4, N / 4, y,
-                                                  ldy, scale, shift, res, ldr, relu, out_bf16);
+                                                  ldy, scale, shift, res, ldr, relu);
   return (int)cudaGetLastError();
 }
 
