@@ -345,3 +345,23 @@ def test_empty_and_invalid(ob, ctx):
         ob.MatMul().compute([torch.zeros((2, 3), device="cuda"), torch.zeros((4, 5), device="cuda")], ctx)
     with pytest.raises(ob.ValidationError):
         ob.Add().compute([torch.zeros((2, 3), device="cuda"), torch.zeros((3, 2), device="cuda")], ctx)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("shape,cpad", [((2, 3, 224, 224), 4), ((3, 1, 8, 12), 4), ((2, 2, 5, 7), 4),
+                                        ((2, 3, 6, 6), 8), ((1, 5, 4, 4), 8), ((2, 40, 9, 7), 40)])
+def test_nchw_to_nhwc_repack(ob, handle, shape, cpad):
+    """Layout repack at the graph edge: NCHW -> channel-padded NHWC, bit-exact with
+    zero padding channels (four-pixel vectors when HW % 4 == 0, other paths otherwise)."""
+    import ctypes
+    C = __import__("importlib").import_module("onnx-rs_b200._capi")
+    rng = np.random.default_rng(17)
+    x = rng.standard_normal(shape).astype(np.float32)
+    n, c, hh, ww = shape
+    xd = cu(x)
+    y = torch.full((n, hh, ww, cpad), 7.0, dtype=torch.float32, device="cuda")
+    handle.check(C.lib().onnxb200_nchw_to_nhwc(handle.ptr, n, c, hh, ww, cpad, ctypes.c_void_p(xd.data_ptr()),
+                                               ctypes.c_void_p(y.data_ptr())), "repack")
+    ref = np.zeros((n, hh, ww, cpad), np.float32)
+    ref[..., :c] = x.transpose(0, 2, 3, 1)
+    np.testing.assert_array_equal(np_(y), ref)
