@@ -1366,18 +1366,22 @@ static int run_steps(onnxb200_graph* g, const float* const* uin, float* const* u
 // Algorithmic work of one step: FLOPs of contractions, and bytes = every input
 // read once + the output written once (fp32).
 static void step_work(const onnxb200_graph* g, const Step& s, int* kind, double* flops, double* bytes) {
-  auto tb = [&](int id) -> double {
-    const GTensor& t = g->tensors[id];
-    return (double)t.numel() * (t.bf16 ? 2.0 : 4.0);
-  };
+  // bytes as stored (channel padding and bf16 storage included)
+  auto tb = [&](int id) -> double { return (double)g->tensors[id].bytes(); };
   *flops = 0;
   *bytes = 0;
   for (int t : s.in)
     if (t >= 0) *bytes += tb(t);
   if (s.out >= 0) *bytes += tb(s.out);
   switch (s.type) {
-    case kInConvert:
-    case kOutConvert:
+    case kInConvert:   // plus the read of the caller's NCHW fp32 buffer
+      *bytes += (double)g->tensors[s.out].numel() * 4.0;
+      *kind = ONNXB200_STEP_CONVERT;
+      break;
+    case kOutConvert:  // plus the write of the caller's fp32 buffer
+      if (!s.in.empty() && s.in[0] >= 0) *bytes += (double)g->tensors[s.in[0]].numel() * 4.0;
+      *kind = ONNXB200_STEP_CONVERT;
+      break;
     case kFlattenCvt:
       *kind = ONNXB200_STEP_CONVERT;
       break;
