@@ -175,11 +175,12 @@ static void choose_tiling(onnxb200_handle* h, onnxb200_conv_plan* p, bool residu
   q.num_kb = p->num_kb;
   q.a_bf16 = p->a_bf16;
   q.out_bf16 = p->out_bf16;
-  int bn = 128, ks = 1;
-  igemm_pick_split(q, residual, p->prec, h->num_sms, &bn, &ks);
+  int bn = 128, ks = 1, smt = 0;
+  igemm_pick_split(q, residual, p->prec, h->num_sms, &bn, &ks, &smt);
   p->bn = bn;
   p->ksplit = ks;
-  p->split_bytes = ks > 1 ? (size_t)ks * q.M * q.Nc * sizeof(float) : 0;
+  p->split_mt = smt;
+  p->split_bytes = ks > 1 ? (size_t)ks * (q.M - smt * 128) * q.Nc * sizeof(float) : 0;
 }
 
 void conv_plan_free(onnxb200_conv_plan* p) {
@@ -355,9 +356,9 @@ int conv_plan_exec_nhwc(onnxb200_handle* h, const onnxb200_conv_plan* p, const f
       if (er) return set_error(h, ONNXB200_ERR_EXECUTION, "Conv: A tensor map encode failed: " + std::to_string(er));
     }
     float* ws = split_ws ? split_ws : p->split_ws;
-    rc = igemm_launch_split(q, ws ? p->ksplit : 1, ws, p->tm_hi, p->tm_lo, am, am, p->prec, p->bn, h->num_sms,
-                            h->stream);
-    if (ws && p->ksplit > 1) h->launches++;  // the reduction pass
+    rc = igemm_launch_split(q, ws ? p->ksplit : 1, p->split_mt, ws, p->tm_hi, p->tm_lo, am, am, p->prec, p->bn,
+                            h->num_sms, h->stream);
+    if (ws && p->ksplit > 1) h->launches += p->split_mt > 0 ? 2 : 1;  // the reduction pass (and tail launch)
   } else {
     rc = conv_direct_launch(x, (int)d.n, (int)d.h, (int)d.w, (int)d.c, p->cs_in, p->w_oihw,
                             (int)d.c_out, (int)d.kh, (int)d.kw, (int)d.stride_h, (int)d.stride_w,
@@ -511,9 +512,9 @@ int conv_dual_exec_nhwc(onnxb200_handle* h, const onnxb200_conv_plan* p, const f
   if (!er) er = encode_a_map(v, q.a_mode2 == kALoadTma2d ? (int)d.n * q.H2 * q.W2 : (int)d.n, &am2);
   if (er) return set_error(h, ONNXB200_ERR_EXECUTION, "Conv: A tensor map encode failed: " + std::to_string(er));
   float* ws = split_ws ? split_ws : p->split_ws;
-  const int rc = igemm_launch_split(q, ws ? p->ksplit : 1, ws, p->tm_hi, p->tm_lo, am, am2, p->prec, p->bn,
-                                    h->num_sms, h->stream);
-  h->launches += (ws && p->ksplit > 1) ? 2 : 1;
+  const int rc = igemm_launch_split(q, ws ? p->ksplit : 1, p->split_mt, ws, p->tm_hi, p->tm_lo, am, am2,
+                                    p->prec, p->bn, h->num_sms, h->stream);
+  h->launches += (ws && p->ksplit > 1) ? (p->split_mt > 0 ? 3 : 2) : 1;
   if (rc) return cuda_check(h, (cudaError_t)rc, "Conv launch");
   return ONNXB200_OK;
 }
@@ -547,13 +548,14 @@ int gemm_tc_run(onnxb200_handle* h, const GemmCall& c, const void* b_hi, const v
   q.ldr = c.ldr;
   q.relu = c.relu;
   q.status = h->d_status;
-  int bn = igemm_pick_bn(q, prec, h->num_sms), ks = 1;
+  int bn = igemm_pick_bn(q, prec, h->num_sms), ks = 1, smt = 0;
   if (c.split_ws) {
-    int b2 = bn, k2 = 1;
-    igemm_pick_split(q, q.res != nullptr, prec, h->num_sms, &b2, &k2);
-    if (k2 > 1 && (size_t)k2 * q.M * q.Nc * sizeof(float) <= c.split_bytes) {
+    int b2 = bn, k2 = 1, m2 = 0;
+    igemm_pick_split(q, q.res != nullptr, prec, h->num_sms, &b2, &k2, &m2);
+    if (k2 > 1 && (size_t)k2 * (q.M - m2 * 128) * q.Nc * sizeof(float) <= c.split_bytes) {
       bn = b2;
       ks = k2;
+      smt = m2;
     }
   }
   q.m_tiles = (q.M + 127) / 128;
@@ -569,8 +571,8 @@ int gemm_tc_run(onnxb200_handle* h, const GemmCall& c, const void* b_hi, const v
     const int er = encode_a_map(q, c.a_rows > 0 ? c.a_rows : c.M, &am);
     if (er) return set_error(h, ONNXB200_ERR_EXECUTION, "GEMM: A tensor map encode failed: " + std::to_string(er));
   }
-  rc = igemm_launch_split(q, ks, c.split_ws, thi, tlo, am, am, prec, bn, h->num_sms, h->stream);
-  h->launches += ks > 1 ? 2 : 1;
+  rc = igemm_launch_split(q, ks, smt, c.split_ws, thi, tlo, am, am, prec, bn, h->num_sms, h->stream);
+  h->launches += ks > 1 ? (smt > 0 ? 3 : 2) : 1;
   if (rc) return cuda_check(h, (cudaError_t)rc, "GEMM launch");
   return ONNXB200_OK;
 }
@@ -582,9 +584,9 @@ size_t gemm_split_bytes(const onnxb200_handle* h, int M, int N, int kpad, int pr
   q.Nc = N;
   q.batches = 1;
   q.num_kb = kpad / igemm_block_k(prec);
-  int bn = 128, ks = 1;
-  igemm_pick_split(q, residual, prec, h->num_sms, &bn, &ks);
-  return ks > 1 ? (size_t)ks * M * N * sizeof(float) : 0;
+  int bn = 128, ks = 1, smt = 0;
+  igemm_pick_split(q, residual, prec, h->num_sms, &bn, &ks, &smt);
+  return ks > 1 ? (size_t)ks * (M - smt * 128) * N * sizeof(float) : 0;
 }
 
 }  // namespace ob2

@@ -6,6 +6,7 @@
 // (src/ops/nn/conv.rs:1142-1368), its direct 1x1 path (conv.rs:849-935 via the
 // SIMD strategy), compute_matmul's per-batch sgemm (src/ops/math/matmul.rs:124-279)
 // and compute_gemm (src/ops/math/gemm.rs:172-291).
+#include <algorithm>
 #include <cuda_runtime.h>
 
 #include "kernels.h"
@@ -90,69 +91,104 @@ int igemm_launch(const IgemmParams& p, const CUtensorMap& hi, const CUtensorMap&
   return (int)cudaErrorInvalidValue;
 }
 
-int igemm_launch_split(const IgemmParams& p, int ksplit, float* ws, const CUtensorMap& hi,
+int igemm_launch_split(const IgemmParams& p, int ksplit, int split_mt, float* ws, const CUtensorMap& hi,
                        const CUtensorMap& lo, const CUtensorMap& am, const CUtensorMap& am2, int precision,
                        int bn, int num_sms, cudaStream_t st) {
   if (ksplit <= 1) return igemm_launch(p, hi, lo, am, am2, precision, bn, num_sms, st);
+  const int m_tiles = (p.M + kBM - 1) / kBM;
   if (!ws || (reinterpret_cast<uintptr_t>(ws) & 15) || p.batches != 1 || p.a_off || p.b_row || p.a_bf16 ||
-      p.out_bf16 || p.num_kb % ksplit)
+      p.out_bf16 || p.num_kb % ksplit || p.m_base || split_mt < 0 || split_mt >= m_tiles)
     return (int)cudaErrorInvalidValue;
-  // slice b's raw sums -> ws[b][M][Nc]
+  int rc = 0;
+  const int m0 = split_mt * kBM;
+  if (split_mt > 0) {  // the whole waves of tiles, unsplit, with the full epilogue
+    IgemmParams h = p;
+    h.M = m0;
+    h.m_tiles = split_mt;
+    rc = igemm_launch(h, hi, lo, am, am2, precision, bn, num_sms, st);
+    if (rc) return rc;
+  }
+  // the tail rows [m0, M): slice b's raw sums -> ws[b][M - m0][Nc]
+  const int mt_rows = p.M - m0;
   IgemmParams q = p;
+  q.m_base = m0;
+  q.M = mt_rows;
+  q.m_tiles = m_tiles - split_mt;
   q.ksplit = ksplit;
   q.batches = ksplit;
   q.y = ws;
   q.ldy = p.Nc;
-  q.y_bstride = (long long)p.M * p.Nc;
+  q.y_bstride = (long long)mt_rows * p.Nc;
   q.scale = q.shift = q.res = nullptr;
   q.relu = 0;
   q.out_bf16 = 0;
-  int rc = igemm_launch(q, hi, lo, am, am2, precision, bn, num_sms, st);
+  rc = igemm_launch(q, hi, lo, am, am2, precision, bn, num_sms, st);
   if (rc) return rc;
-  return splitk_reduce_launch(ws, ksplit, p.M, p.Nc, p.y, p.ldy, p.scale, p.shift, p.res, p.ldr, p.relu, st);
+  return splitk_reduce_launch(ws, ksplit, mt_rows, p.Nc, p.y + (long long)m0 * p.ldy, p.ldy, p.scale, p.shift,
+                              p.res ? p.res + (long long)m0 * p.ldr : nullptr, p.ldr, p.relu, st);
 }
 
-void igemm_pick_split(const IgemmParams& p, bool residual, int precision, int num_sms, int* bn, int* ksplit) {
+void igemm_pick_split(const IgemmParams& p, bool residual, int precision, int num_sms, int* bn, int* ksplit,
+                      int* split_mt) {
   const int bn0 = igemm_pick_bn(p, precision, num_sms);
   *bn = bn0;
   *ksplit = 1;
+  *split_mt = 0;
   if (p.batches != 1 || p.a_off || p.b_row || p.a_bf16 || p.out_bf16 || p.num_kb < 8 || num_sms <= 0) return;
   // modelled time in units of one k-block of a 128-column tile; a 64-column
   // tile's k-block costs ~0.8 of it (its MMAs are half as long, the operand
   // round trip is not)
   const double kb_us = precision == kPrec3xTF32 ? 0.8 : 0.5;
   const long long mt = (p.M + kBM - 1) / kBM;
-  auto cost = [&](int b, int s) {
-    const long long tiles = mt * ((p.Nc + b - 1) / b);
+  // M-tiles [m_from, m_to) with tile width b, K split s (1 = none)
+  auto cost = [&](int b, int s, long long m_from, long long m_to) {
+    const long long tiles = (m_to - m_from) * ((p.Nc + b - 1) / b);
     const long long waves = (tiles * s + num_sms - 1) / num_sms;
     double c = (double)waves * (p.num_kb / s) * (b == 64 ? 0.8 : 1.0);
     if (s > 1) {  // reduction pass: read the s slices (from L2 when they fit it,
                   // ~10 TB/s), read the residual and write y from / to HBM (~6 TB/s)
-      const double slice = (double)p.M * p.Nc * 4.0;
+      const double rows = (double)std::min<long long>(p.M, m_to * kBM) - (double)(m_from * kBM);
+      const double slice = rows * p.Nc * 4.0;
       const double ws_gbs = s * slice <= 64e6 ? 10.0e6 : 6.0e6;  // bytes per us
       c += (s * slice / ws_gbs + (1 + (residual ? 1 : 0)) * slice / 6.0e6 + 2.0) / kb_us;
     }
     return c;
   };
-  double best = cost(bn0, 1);
-  const double unsplit = best;
-  int best_bn = bn0, best_s = 1;
+  const double unsplit = cost(bn0, 1, 0, mt);
+  double best = unsplit;
+  int best_bn = bn0, best_s = 1, best_mt = 0;
   const int cands[2] = {bn0, (bn0 == 64 && p.Nc > 64 && precision != kPrecTF32) ? 128 : 0};
   for (int b : cands) {
     if (!b) continue;
+    const long long nt = (p.Nc + b - 1) / b;
+    // tail split: the whole waves of tiles (whole M-tiles of them) unsplit, the
+    // remaining M-tiles split, in a second launch (+~3 us)
+    const long long full = (mt * nt) / num_sms * num_sms;
+    const long long mt0 = full / nt;
     for (int s = 2; s <= 16; ++s) {
       if (p.num_kb % s || p.num_kb / s < 4) continue;
-      const double c = cost(b, s);
-      if (c < best) {
-        best = c;
+      const double c_all = cost(b, s, 0, mt);
+      if (c_all < best) {
+        best = c_all;
         best_bn = b;
         best_s = s;
+        best_mt = 0;
+      }
+      if (mt0 > 0 && mt0 < mt) {
+        const double c_tail = cost(b, 1, 0, mt0) + cost(b, s, mt0, mt) + 3.0 / kb_us;
+        if (c_tail < best) {
+          best = c_tail;
+          best_bn = b;
+          best_s = s;
+          best_mt = (int)mt0;
+        }
       }
     }
   }
-  if (best_s > 1 && best < 0.9 * unsplit) {
+  if (best_s > 1 && best < 0.94 * unsplit) {
     *bn = best_bn;
     *ksplit = best_s;
+    *split_mt = best_mt;
   }
 }
 

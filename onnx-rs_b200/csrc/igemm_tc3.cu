@@ -311,9 +311,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           int a_r0 = 0, a_x = 0, a_y = 0, a_n = 0;
           uint16_t off_w[kBK / 4], off_h[kBK / 4];  // im2col tap offsets (<= 8 taps per k-block)
           if (p.a_mode == kALoadTma2d) {
-            a_r0 = (p.a_off ? (int)(p.a_off[b] / p.Cs) : 0) + mt * kBM;
+            a_r0 = (p.a_off ? (int)(p.a_off[b] / p.Cs) : 0) + p.m_base + mt * kBM;
           } else {
-            const int m0 = mt * kBM;
+            const int m0 = p.m_base + mt * kBM;
             a_n = m0 / OHW;
             const int rem = m0 - a_n * OHW;
             const int oh0 = rem / p.OW;
@@ -332,7 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const bool src2 = p.kb_split && kb >= p.kb_split;
           int b_x = 0, b_y = 0, b_n = 0;
           if (src2 && p.a_mode2 != kALoadTma2d) {
-            const int m0 = mt * kBM;
+            const int m0 = p.m_base + mt * kBM;
             b_n = m0 / OHW;
             const int rem = m0 - b_n * OHW;
             const int oh0 = rem / p.OW;
@@ -344,7 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (src2) {
             const int k2 = (kb - p.kb_split) * kBK;
             if (p.a_mode2 == kALoadTma2d)
-              tma_load_2d(dst, &tm_a2, k2, mt * kBM, s1_full(s));
+              tma_load_2d(dst, &tm_a2, k2, p.m_base + mt * kBM, s1_full(s));
             else
               tma_load_im2col_4d(dst, &tm_a2, k2, b_x, b_y, b_n, 0, 0, s1_full(s));
           } else if (p.a_mode == kALoadTma2d) {
@@ -381,8 +381,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 8; ++i) {
             const int m = mt * kBM + rslot + 16 * i;
             if (m < p.M) {
-              const int n = m / OHW;
-              const int rem = m - n * OHW;
+              const int n = (p.m_base + m) / OHW;
+              const int rem = p.m_base + m - n * OHW;
               const int oh = rem / p.OW;
               const int ow = rem - oh * p.OW;
               pix[i] = n * p.Hin * p.Win;

@@ -62,6 +62,7 @@ struct onnxb200_conv_plan {
   // the plan's own (split_ws, op-level plans) or one the caller passes (graphs);
   // with neither the plan runs unsplit.
   int ksplit = 1;
+  int split_mt = 0;          // first split M-tile (0 = all; > 0: only the last wave's)
   size_t split_bytes = 0;
   float* split_ws = nullptr;
 };

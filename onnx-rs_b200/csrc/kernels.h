@@ -63,6 +63,10 @@ struct IgemmParams {
   // problem is then `ksplit` batches over the same A and B (batches == ksplit),
   // batch b running k-blocks [b * num_kb / ksplit, (b + 1) * num_kb / ksplit).
   int ksplit;
+  // Output rows of A (pixels) before this problem's row 0: a problem that is the
+  // tail of a larger one reads A (and computes pixel coordinates) at rows
+  // m_base + m, while y, the residual and M stay relative to the tail.
+  int m_base;
 };
 
 enum ALoadMode { kALoadGather = 0, kALoadTma2d = 1, kALoadIm2col = 2, kALoadIm2colTaps = 3 };
@@ -101,15 +105,21 @@ int igemm3_launch(const IgemmParams& p, const CUtensorMap& tm_hi, const CUtensor
 // aligned), then one reduction pass sums the slices in order and applies p's
 // epilogue (scale, shift, residual, Relu) into p.y.  ksplit <= 1 is a plain
 // igemm_launch.  Single-batch problems with fp32 activations and outputs only.
-int igemm_launch_split(const IgemmParams& p, int ksplit, float* ws, const CUtensorMap& tm_hi,
+// split_mt > 0 splits only the tail: M-tiles [0, split_mt) run unsplit first (the
+// whole waves of tiles), then rows [split_mt * 128, M) run split, ws holding
+// [ksplit][M - split_mt * 128][Nc].
+int igemm_launch_split(const IgemmParams& p, int ksplit, int split_mt, float* ws, const CUtensorMap& tm_hi,
                        const CUtensorMap& tm_lo, const CUtensorMap& tm_a, const CUtensorMap& tm_a2,
                        int precision, int bn, int num_sms, cudaStream_t stream);
 
 // Tile width and K split for a problem (geometry in p; `residual`: the epilogue
 // adds a residual): igemm_pick_bn's width, or (when a K split is modelled to be
-// >= 10% faster: few output tiles, long K) the split and the width to use with
+// >= 6% faster: few output tiles or a partial last wave, long K) the split and the width to use with
 // it.  *ksplit = 1 means no split.  Only fp32 activations and outputs split.
-void igemm_pick_split(const IgemmParams& p, bool residual, int precision, int num_sms, int* bn, int* ksplit);
+// *split_mt: the first split M-tile (0 = the whole problem; > 0: only the tail
+// past the whole waves of tiles).
+void igemm_pick_split(const IgemmParams& p, bool residual, int precision, int num_sms, int* bn, int* ksplit,
+                      int* split_mt);
 
 // Sums ksplit slices of [M][N] fp32 partial sums (slice order) and applies the
 // epilogue: y = relu(sum * scale + shift + res), all fp32.
