@@ -43,11 +43,12 @@ METRIC = "ResNet-50 v1.5 images/sec (batch 256, fp32 via 3xTF32)"
 METRIC_FAST = {"tf32": "ResNet-50 v1.5 images/sec (batch 256, fast mode: 1xTF32)",
                "bf16": "ResNet-50 v1.5 images/sec (batch 256, fast mode: BF16)",
                "fp32": "ResNet-50 v1.5 images/sec (batch 256, fp32 on CUDA cores)"}
-# DRAM bytes per igemm_tc3_kernel launch, mean over the 50 launches of one
-# batch-256 3xTF32 run (49 convolution steps and the classifier Gemm):
-# dram__bytes_read.sum + dram__bytes_write.sum from an ncu DRAM capture of this
-# workload (a measured constant, not re-derived here).
-TRAFFIC_PER_LAUNCH_3XTF32 = 446.8e6
+# DRAM bytes of igemm_tc3_kernel per contraction step, mean over the 50 steps
+# of one batch-256 3xTF32 run (49 convolution steps and the classifier Gemm; a
+# step whose K loop is split runs two or three launches, all counted):
+# dram__bytes_read.sum + dram__bytes_write.sum over the run's 59 launches from an
+# ncu DRAM capture of this workload (a measured constant, not re-derived here).
+TRAFFIC_PER_LAUNCH_3XTF32 = 447.5e6
 L2_BYTES = 126 * 1024 * 1024
 
 
@@ -326,9 +327,9 @@ def roofline_of(prof, peaks, peak_src, precision, traffic=None):
             "frac": achieved / burst if burst else None,
             "peak_sustained": sus, "frac_of_sustained": achieved / sus if sus else None,
             "traffic": traffic,
-            "traffic_note": "DRAM bytes per contraction launch (mean over the run's launches) from one ncu "
-                            "DRAM capture of this workload" if traffic else None,
-            "kernel": kernel + " (all Conv/Gemm launches of one run)",
+            "traffic_note": "DRAM bytes per contraction step (mean over the run's steps, a K-split step's "
+                            "launches together) from one ncu DRAM capture of this workload" if traffic else None,
+            "kernel": kernel + " (all Conv/Gemm steps of one run)",
             "launches": len(tc), "flops_per_launch": tc_flops / max(1, len(tc)),
             "peak_source": f"{peak_src} ({'MEASURED_PEAKS.json' if peak_src == 'measured' else 'fallback'}): "
                            f"{basis}; `peak` = burst (bf16_tflops), `peak_sustained` = bf16_tflops_sustained",
