@@ -187,6 +187,28 @@ def test_conv_fused_bn_residual_relu(ob, oracle, ctx):
     assert_close(y, ref, 1e-5, 1e-4, "conv+bn+add+relu")
 
 
+def test_conv_tail_split_bn_residual(ob, oracle, ctx):
+    """3x3 256->256 at 14x14, 64 images, folded BN + residual + Relu: 196 output tiles
+    (1.3 waves), so the first wave runs whole and the last M-tiles run as a K-split
+    launch whose reduction pass applies the scale, shift, residual and Relu.  Images
+    at both ends (the split rows are the last ones) against the oracle."""
+    rng = np.random.default_rng(18)
+    x = rng.standard_normal((64, 256, 14, 14)).astype(np.float32)
+    w = (rng.standard_normal((256, 256, 3, 3)) * np.sqrt(2.0 / 2304)).astype(np.float32)
+    b = rng.uniform(-0.1, 0.1, 256).astype(np.float32)
+    gamma = rng.uniform(0.5, 1.5, 256).astype(np.float32)
+    beta = rng.uniform(-0.2, 0.2, 256).astype(np.float32)
+    mean = rng.normal(0, 0.1, 256).astype(np.float32)
+    var = rng.uniform(0.5, 1.5, 256).astype(np.float32)
+    res = rng.standard_normal((64, 256, 14, 14)).astype(np.float32)
+    y = run_conv(ob, ctx, x, w, b, {"pads": (1, 1, 1, 1)}, "3xtf32", relu=True,
+                 bn=(gamma, beta, mean, var, 1e-5), residual=res)
+    imgs = [0, 1, 37, 52, 60, 61, 62, 63]
+    c = oracle.conv2d(np.ascontiguousarray(x[imgs]), w, b, (1, 1), (1, 1, 1, 1))
+    ref = oracle.relu(oracle.add(oracle.batchnorm(c, gamma, beta, mean, var, 1e-5), res[imgs]))
+    assert_close(y[imgs], ref, 1e-5, 1e-4, f"tail split {imgs}")
+
+
 SWEEP_NAMES = [s[0] for s in __import__("importlib").import_module("onnx-rs_b200").workloads.SWEEP]
 
 
