@@ -391,62 +391,162 @@ int conv_direct_launch(const float* x, int N, int H, int W, int C, int Cs, const
 }
 
 // ------------------------------------------------------------------ SIMT GEMM
-// 64x64 tile, 256 threads, 4x4 outputs per thread, fp32 FFMA.
-__global__ void gemm_simt_kernel(const float* __restrict__ a, const float* __restrict__ b,
-                                 const long long* a_off, const long long* b_off,
-                                 long long y_bstride, int M, int N, int K, int lda, int ldb,
-                                 int ta, int tb, const float* __restrict__ scale,
-                                 const float* __restrict__ shift, const float* __restrict__ res,
-                                 int ldr, int relu, float* __restrict__ y, int ldy) {
-  __shared__ float As[16][64 + 1];
-  __shared__ float Bs[16][64 + 1];
+// fp32 FFMA GEMM for the exact-fp32 precision mode and for shapes the tensor-core
+// path refuses.  A 256-thread block owns a 128 x 128 output tile; a thread owns
+// 8 x 8 outputs as two 4-row groups 64 rows apart times two 4-column groups 64
+// columns apart, so that a warp's shared-memory reads are conflict-free 16-byte
+// vectors.  K advances 8 at a time: the next step's A and B tiles are read into
+// registers (16-byte global loads where the operand's pointer and leading
+// dimension allow) while the current step's tiles are multiplied from the other
+// shared-memory buffer.  Every output sums its K products in order, k = 0, 1, ...,
+// with fmaf.
+constexpr int kSgBM = 128, kSgBN = 128, kSgBK = 8;
+
+__device__ __forceinline__ bool aligned16(const void* p) {
+  return (reinterpret_cast<uintptr_t>(p) & 15) == 0;
+}
+
+__global__ void __launch_bounds__(256, 2)
+gemm_simt_kernel(const float* __restrict__ a, const float* __restrict__ b, const long long* a_off,
+                 const long long* b_off, long long y_bstride, int M, int N, int K, int lda, int ldb,
+                 int ta, int tb, const float* __restrict__ scale, const float* __restrict__ shift,
+                 const float* __restrict__ res, int ldr, int relu, float* __restrict__ y, int ldy) {
+  __shared__ __align__(16) float As[2][kSgBK][kSgBM];
+  __shared__ __align__(16) float Bs[2][kSgBK][kSgBN];
   const int bz = blockIdx.z;
   const float* A = a + (a_off ? a_off[bz] : 0);
   const float* B = b + (b_off ? b_off[bz] : 0);
   float* Y = y + (long long)bz * y_bstride;
   const float* R = res ? res + (long long)bz * y_bstride : nullptr;
-  const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
-  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
-  float acc[4][4] = {};
-  for (int k0 = 0; k0 < K; k0 += 16) {
-    for (int i = threadIdx.x; i < 16 * 64; i += 256) {
-      const int kk = i / 64, mm = i % 64;
-      const int gm = m0 + mm, gk = k0 + kk;
-      float v = 0.f;
-      if (gm < M && gk < K) v = ta ? A[(long long)gk * lda + gm] : A[(long long)gm * lda + gk];
-      As[kk][mm] = v;
-      const int gn = n0 + mm;
-      float u = 0.f;
-      if (gn < N && gk < K) u = tb ? B[(long long)gn * ldb + gk] : B[(long long)gk * ldb + gn];
-      Bs[kk][mm] = u;
+  const int m0 = blockIdx.y * kSgBM, n0 = blockIdx.x * kSgBN;
+  const int t = threadIdx.x, tx = t % 16, ty = t / 16;
+  const bool va = (lda & 3) == 0 && aligned16(A);
+  const bool vb = (ldb & 3) == 0 && aligned16(B);
+  // This thread's share of a K step: four A values and four B values, either
+  // four consecutive k of one row (operand stored with k contiguous) or one k of
+  // four consecutive rows (operand stored with rows contiguous).
+  const int a_r = ta ? (t % 32) * 4 : t / 2, a_k = ta ? t / 32 : (t % 2) * 4;
+  const int b_r = tb ? t / 2 : (t % 32) * 4, b_k = tb ? (t % 2) * 4 : t / 32;
+  float ra[4], rb[4];
+  auto load = [&](int k0) {
+    if (!ta) {  // A[m][k]: k contiguous
+      const int m = m0 + a_r, k = k0 + a_k;
+      const float* src = A + (long long)m * lda + k;
+      if (m < M && va && k + 3 < K) {
+        const float4 v = *reinterpret_cast<const float4*>(src);
+        ra[0] = v.x; ra[1] = v.y; ra[2] = v.z; ra[3] = v.w;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) ra[i] = (m < M && k + i < K) ? src[i] : 0.f;
+      }
+    } else {  // A[k][m]: m contiguous
+      const int m = m0 + a_r, k = k0 + a_k;
+      const float* src = A + (long long)k * lda + m;
+      if (k < K && va && m + 3 < M) {
+        const float4 v = *reinterpret_cast<const float4*>(src);
+        ra[0] = v.x; ra[1] = v.y; ra[2] = v.z; ra[3] = v.w;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) ra[i] = (k < K && m + i < M) ? src[i] : 0.f;
+      }
     }
-    __syncthreads();
+    if (!tb) {  // B[k][n]: n contiguous
+      const int n = n0 + b_r, k = k0 + b_k;
+      const float* src = B + (long long)k * ldb + n;
+      if (k < K && vb && n + 3 < N) {
+        const float4 v = *reinterpret_cast<const float4*>(src);
+        rb[0] = v.x; rb[1] = v.y; rb[2] = v.z; rb[3] = v.w;
+      } else {
 #pragma unroll
-    for (int kk = 0; kk < 16; ++kk) {
-      float av[4], bv[4];
+        for (int i = 0; i < 4; ++i) rb[i] = (k < K && n + i < N) ? src[i] : 0.f;
+      }
+    } else {  // B[n][k]: k contiguous
+      const int n = n0 + b_r, k = k0 + b_k;
+      const float* src = B + (long long)n * ldb + k;
+      if (n < N && vb && k + 3 < K) {
+        const float4 v = *reinterpret_cast<const float4*>(src);
+        rb[0] = v.x; rb[1] = v.y; rb[2] = v.z; rb[3] = v.w;
+      } else {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) av[i] = As[kk][ty * 4 + i];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) bv[j] = Bs[kk][tx * 4 + j];
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        for (int i = 0; i < 4; ++i) rb[i] = (n < N && k + i < K) ? src[i] : 0.f;
+      }
     }
+  };
+  auto store = [&](int buf) {
+    if (!ta) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) As[buf][a_k + i][a_r] = ra[i];
+    } else {
+      *reinterpret_cast<float4*>(&As[buf][a_k][a_r]) = make_float4(ra[0], ra[1], ra[2], ra[3]);
+    }
+    if (tb) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) Bs[buf][b_k + i][b_r] = rb[i];
+    } else {
+      *reinterpret_cast<float4*>(&Bs[buf][b_k][b_r]) = make_float4(rb[0], rb[1], rb[2], rb[3]);
+    }
+  };
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+  if (K > 0) {
+    load(0);
+    store(0);
+  }
+  __syncthreads();
+  for (int k0 = 0, buf = 0; k0 < K; k0 += kSgBK, buf ^= 1) {
+    const bool more = k0 + kSgBK < K;
+    if (more) load(k0 + kSgBK);
+#pragma unroll
+    for (int kk = 0; kk < kSgBK; ++kk) {
+      float av[8], bv[8];
+      const float4 a0 = *reinterpret_cast<const float4*>(&As[buf][kk][ty * 4]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&As[buf][kk][ty * 4 + 64]);
+      const float4 b0 = *reinterpret_cast<const float4*>(&Bs[buf][kk][tx * 4]);
+      const float4 b1 = *reinterpret_cast<const float4*>(&Bs[buf][kk][tx * 4 + 64]);
+      av[0] = a0.x; av[1] = a0.y; av[2] = a0.z; av[3] = a0.w;
+      av[4] = a1.x; av[5] = a1.y; av[6] = a1.z; av[7] = a1.w;
+      bv[0] = b0.x; bv[1] = b0.y; bv[2] = b0.z; bv[3] = b0.w;
+      bv[4] = b1.x; bv[5] = b1.y; bv[6] = b1.z; bv[7] = b1.w;
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+    // the buffer written here was last read in the previous step, before the
+    // barrier that ended it; the barrier below publishes it for the next step
+    if (more) store(buf ^ 1);
     __syncthreads();
   }
+  const bool vy = (ldy & 3) == 0 && aligned16(Y) && (!R || ((ldr & 3) == 0 && aligned16(R)));
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int gm = m0 + ty * 4 + i;
+  for (int i = 0; i < 8; ++i) {
+    const int gm = m0 + ty * 4 + (i & 3) + (i >> 2) * 64;
     if (gm >= M) continue;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int gn = n0 + tx * 4 + j;
+    for (int jg = 0; jg < 2; ++jg) {
+      const int gn = n0 + tx * 4 + jg * 64;
       if (gn >= N) continue;
-      float v = epi(acc[i][j], scale, shift, gn);
-      if (R) v += R[(long long)gm * ldr + gn];
-      if (relu) v = v > 0.f ? v : 0.f;
-      Y[(long long)gm * ldy + gn] = v;
+      float v[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        v[j] = 0.f;
+        if (gn + j < N) {
+          v[j] = epi(acc[i][jg * 4 + j], scale, shift, gn + j);
+          if (R) v[j] += R[(long long)gm * ldr + gn + j];
+          if (relu) v[j] = v[j] > 0.f ? v[j] : 0.f;
+        }
+      }
+      float* dst = Y + (long long)gm * ldy + gn;
+      if (vy && gn + 3 < N) {
+        *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (gn + j < N) dst[j] = v[j];
+      }
     }
   }
 }
@@ -456,7 +556,7 @@ int gemm_simt_launch(const float* a, const float* b, int batches, const long lon
                      int ldb, int ta, int tb, const float* scale, const float* shift,
                      const float* res, int ldr, int relu, float* y, int ldy, cudaStream_t st) {
   if (M == 0 || N == 0 || batches == 0) return 0;
-  dim3 grid((N + 63) / 64, (M + 63) / 64, batches);
+  dim3 grid((N + kSgBN - 1) / kSgBN, (M + kSgBM - 1) / kSgBM, batches);
   gemm_simt_kernel<<<grid, 256, 0, st>>>(a, b, a_off, b_off, y_bstride, M, N, K, lda, ldb, ta, tb,
                                           scale, shift, res, ldr, relu, y, ldy);
   return (int)cudaGetLastError();
@@ -1041,17 +1141,37 @@ int conv3d_direct_launch(const float* x, const float* w, const float* bias, floa
 }
 
 // relu (src/ops/activations.rs:244-246): v > 0 ? v : 0 (NaN -> 0).
+__device__ __forceinline__ float relu1(float v) { return v > 0.f ? v : 0.f; }
+
 __global__ void relu_kernel(const float* __restrict__ x, float* __restrict__ y, long long n) {
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x)
+    y[i] = relu1(x[i]);
+}
+
+// 16-byte vectors over the first n & ~3 elements (both pointers 16-byte aligned);
+// the first threads of block 0 take the last n & 3.
+__global__ void relu_v4_kernel(const float* __restrict__ x, float* __restrict__ y, long long n) {
+  const long long n4 = n >> 2;
+  const float4* x4 = reinterpret_cast<const float4*>(x);
+  float4* y4 = reinterpret_cast<float4*>(y);
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4;
        i += (long long)gridDim.x * blockDim.x) {
-    const float v = x[i];
-    y[i] = v > 0.f ? v : 0.f;
+    const float4 v = x4[i];
+    y4[i] = make_float4(relu1(v.x), relu1(v.y), relu1(v.z), relu1(v.w));
+  }
+  if (blockIdx.x == 0 && threadIdx.x < (n & 3)) {
+    const long long i = (n4 << 2) + threadIdx.x;
+    y[i] = relu1(x[i]);
   }
 }
 
 int relu_launch(const float* x, float* y, long long n, cudaStream_t st) {
   if (n == 0) return 0;
-  relu_kernel<<<grid_for(n, kBlock), kBlock, 0, st>>>(x, y, n);
+  if (((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15) == 0)
+    relu_v4_kernel<<<grid_for(n >> 2, kBlock), kBlock, 0, st>>>(x, y, n);
+  else
+    relu_kernel<<<grid_for(n, kBlock), kBlock, 0, st>>>(x, y, n);
   return (int)cudaGetLastError();
 }
 

@@ -243,7 +243,7 @@ def test_matmul_reference_cases(ob, oracle, ctx, case, precision):
 
 @pytest.mark.parametrize("sa,sb", [((4, 64, 96), (96, 128)), ((2, 1, 72, 40), (3, 40, 36)),
                                    ((130, 260), (260, 68)), ((5, 200, 32), (5, 32, 260))])
-@pytest.mark.parametrize("precision", ["3xtf32", "tf32", "bf16"])
+@pytest.mark.parametrize("precision", ["3xtf32", "tf32", "bf16", "fp32"])
 def test_matmul_random(ob, oracle, ctx, sa, sb, precision):
     rng = np.random.default_rng(13)
     a = rng.standard_normal(sa).astype(np.float32)
@@ -310,6 +310,21 @@ def test_gemm_attributes(ob, oracle, ctx, ta, tb, cshape, alpha, beta):
     assert_close(np_(y), ref, 1e-5, 1e-4, "gemm")
 
 
+@pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
+@pytest.mark.parametrize("m,n,k", [(37, 129, 61), (130, 260, 264), (8, 1000, 512)])
+def test_gemm_fp32_cuda_cores(ob, oracle, ctx, ta, tb, m, n, k):
+    """fp32 precision (CUDA-core FFMA GEMM): every transpose combination over odd
+    sizes (scalar operand loads and stores at the tile edges), multiples of 4 (16-byte
+    vector loads) and the classifier shape, with alpha, beta and a full C."""
+    rng = np.random.default_rng(21)
+    a = rng.standard_normal((k, m) if ta else (m, k)).astype(np.float32)
+    b = (rng.standard_normal((n, k) if tb else (k, n)) / np.sqrt(k)).astype(np.float32)
+    c = rng.standard_normal((m, n)).astype(np.float32)
+    y = ob.Gemm(0.5, 2.0, ta, tb, precision="fp32").compute([cu(a), cu(b), cu(c)], ctx)[0]
+    ref = oracle.gemm(a, b, c, 0.5, 2.0, ta, tb)
+    assert_close(np_(y), ref, 1e-5, 1e-4, f"gemm fp32 {m}x{n}x{k} ta={ta} tb={tb}")
+
+
 def test_maxpool_and_indices(ob, oracle, ctx):
     rng = np.random.default_rng(15)
     x = rng.standard_normal((4, 64, 112, 112)).astype(np.float32)
@@ -346,6 +361,9 @@ def test_gap_relu_add_bn(ob, oracle, ctx):
     r = rng.standard_normal(100003).astype(np.float32)
     r[5] = np.nan
     np.testing.assert_array_equal(np_(ob.Relu().compute([cu(r)], ctx)[0]), oracle.relu(r))
+    # 4-byte-offset view (one element per thread) and fewer elements than a vector
+    np.testing.assert_array_equal(np_(ob.Relu().compute([cu(r)[1:]], ctx)[0]), oracle.relu(r[1:]))
+    np.testing.assert_array_equal(np_(ob.Relu().compute([cu(r[:3])], ctx)[0]), oracle.relu(r[:3]))
     for sa, sb in [((2, 64, 7, 7), (2, 64, 7, 7)), ((8, 12, 16, 32), (32,)), ((2, 1, 5), (3, 1)), ((7,), ())]:
         a = rng.standard_normal(sa).astype(np.float32)
         b = rng.standard_normal(sb).astype(np.float32)
