@@ -329,6 +329,11 @@ int splitk_reduce_launch(const float* ws, int ksplit, int M, int N, float* y, in
   return (int)cudaGetLastError();
 }
 
+int conv_simt_igemm_launch(const float* x, int N, int H, int W, int C, int Cs, const float* w, int CO,
+                           int KH, int KW, int sh, int sw, int ph, int pw, int dh, int dw, int OH, int OW,
+                           const float* scale, const float* shift, const float* res, int relu, float* y,
+                           cudaStream_t st);
+
 int conv_direct_launch(const float* x, int N, int H, int W, int C, int Cs, const float* w, int CO,
                        int KH, int KW, int sh, int sw, int ph, int pw, int dh, int dw, int group, int OH,
                        int OW, const float* scale, const float* shift, const float* res, int relu,
@@ -384,6 +389,11 @@ int conv_direct_launch(const float* x, int N, int H, int W, int C, int Cs, const
     else go(conv_grouped_v4_kernel<0, 0, 0>);
     return (int)cudaGetLastError();
   }
+  // ungrouped (the fp32 precision mode): implicit GEMM on the CUDA cores
+  const long long npix = (long long)N * OH * OW;
+  if (group == 1 && (npix + 127) / 128 <= 65535 && (long long)C * KH * KW < (1ll << 31))
+    return conv_simt_igemm_launch(x, N, H, W, C, Cs, w, CO, KH, KW, sh, sw, ph, pw, dh, dw, OH, OW,
+                                  scale, shift, res, relu, y, st);
   conv_direct_kernel<<<grid_for(total, kBlock), kBlock, 0, st>>>(
       x, N, H, W, C, Cs, w, CO, KH, KW, sh, sw, ph, pw, dh, dw, group, OH, OW, scale, shift, res,
       relu, y);
@@ -399,18 +409,27 @@ int conv_direct_launch(const float* x, int N, int H, int W, int C, int Cs, const
 // registers (16-byte global loads where the operand's pointer and leading
 // dimension allow) while the current step's tiles are multiplied from the other
 // shared-memory buffer.  Every output sums its K products in order, k = 0, 1, ...,
-// with fmaf.
+// with fmaf.  With kConv the A operand is an ungrouped NHWC convolution's input
+// gathered on the fly (implicit GEMM): row m = output pixel (n, oh, ow), column
+// k = (ci, r, s) in the order of the OIHW weights, which are B as stored
+// ([c_out][k], trans_b); padding taps read as 0.
 constexpr int kSgBM = 128, kSgBN = 128, kSgBK = 8;
+
+struct SimtConvGeom {
+  int H, W, Cs, OH, OW, KH, KW, sh, sw, ph, pw, dh, dw;
+};
 
 __device__ __forceinline__ bool aligned16(const void* p) {
   return (reinterpret_cast<uintptr_t>(p) & 15) == 0;
 }
 
+template <bool kConv>
 __global__ void __launch_bounds__(256, 2)
 gemm_simt_kernel(const float* __restrict__ a, const float* __restrict__ b, const long long* a_off,
                  const long long* b_off, long long y_bstride, int M, int N, int K, int lda, int ldb,
                  int ta, int tb, const float* __restrict__ scale, const float* __restrict__ shift,
-                 const float* __restrict__ res, int ldr, int relu, float* __restrict__ y, int ldy) {
+                 const float* __restrict__ res, int ldr, int relu, float* __restrict__ y, int ldy,
+                 SimtConvGeom g) {
   __shared__ __align__(16) float As[2][kSgBK][kSgBM];
   __shared__ __align__(16) float Bs[2][kSgBK][kSgBN];
   const int bz = blockIdx.z;
@@ -427,9 +446,41 @@ gemm_simt_kernel(const float* __restrict__ a, const float* __restrict__ b, const
   // four consecutive rows (operand stored with rows contiguous).
   const int a_r = ta ? (t % 32) * 4 : t / 2, a_k = ta ? t / 32 : (t % 2) * 4;
   const int b_r = tb ? t / 2 : (t % 32) * 4, b_k = tb ? (t % 2) * 4 : t / 32;
+  // kConv: this thread's output pixel, its filter window origin and its image
+  const float* cx = A;
+  int cih0 = 0, ciw0 = 0;
+  bool cok = false;
+  if constexpr (kConv) {
+    const int m = m0 + a_r;
+    cok = m < M;
+    if (cok) {
+      const int ow = m % g.OW, q = m / g.OW, oh = q % g.OH, n = q / g.OH;
+      cih0 = oh * g.sh - g.ph;
+      ciw0 = ow * g.sw - g.pw;
+      cx = A + (long long)n * g.H * g.W * g.Cs;
+    }
+  }
   float ra[4], rb[4];
   auto load = [&](int k0) {
-    if (!ta) {  // A[m][k]: k contiguous
+    if constexpr (kConv) {  // four consecutive (ci, r, s) of this thread's pixel
+      const int k = k0 + a_k, khw = g.KH * g.KW;
+      int ci = k / khw, rs = k - ci * khw;
+      int r = rs / g.KW, s = rs - r * g.KW;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int ih = cih0 + r * g.dh, iw = ciw0 + s * g.dw;
+        ra[i] = (cok && k + i < K && (unsigned)ih < (unsigned)g.H && (unsigned)iw < (unsigned)g.W)
+                    ? cx[((long long)ih * g.W + iw) * g.Cs + ci]
+                    : 0.f;
+        if (++s == g.KW) {
+          s = 0;
+          if (++r == g.KH) {
+            r = 0;
+            ++ci;
+          }
+        }
+      }
+    } else if (!ta) {  // A[m][k]: k contiguous
       const int m = m0 + a_r, k = k0 + a_k;
       const float* src = A + (long long)m * lda + k;
       if (m < M && va && k + 3 < K) {
@@ -557,8 +608,24 @@ int gemm_simt_launch(const float* a, const float* b, int batches, const long lon
                      const float* res, int ldr, int relu, float* y, int ldy, cudaStream_t st) {
   if (M == 0 || N == 0 || batches == 0) return 0;
   dim3 grid((N + kSgBN - 1) / kSgBN, (M + kSgBM - 1) / kSgBM, batches);
-  gemm_simt_kernel<<<grid, 256, 0, st>>>(a, b, a_off, b_off, y_bstride, M, N, K, lda, ldb, ta, tb,
-                                          scale, shift, res, ldr, relu, y, ldy);
+  gemm_simt_kernel<false><<<grid, 256, 0, st>>>(a, b, a_off, b_off, y_bstride, M, N, K, lda, ldb, ta,
+                                                 tb, scale, shift, res, ldr, relu, y, ldy, SimtConvGeom{});
+  return (int)cudaGetLastError();
+}
+
+// Ungrouped convolution (NHWC input with channel stride Cs, OIHW weights, output
+// [pixel][c_out]) as the implicit GEMM above; the caller keeps N*OH*OW / 128
+// within the grid's y limit and C*KH*KW within int.
+int conv_simt_igemm_launch(const float* x, int N, int H, int W, int C, int Cs, const float* w, int CO,
+                           int KH, int KW, int sh, int sw, int ph, int pw, int dh, int dw, int OH, int OW,
+                           const float* scale, const float* shift, const float* res, int relu, float* y,
+                           cudaStream_t st) {
+  const int M = N * OH * OW, K = C * KH * KW;
+  if (M == 0 || CO == 0) return 0;
+  const SimtConvGeom g{H, W, Cs, OH, OW, KH, KW, sh, sw, ph, pw, dh, dw};
+  dim3 grid((CO + kSgBN - 1) / kSgBN, (M + kSgBM - 1) / kSgBM, 1);
+  gemm_simt_kernel<true><<<grid, 256, 0, st>>>(x, w, nullptr, nullptr, 0, M, CO, K, 0, K, 0, 1, scale,
+                                                shift, res, CO, relu, y, CO, g);
   return (int)cudaGetLastError();
 }
 

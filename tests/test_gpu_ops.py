@@ -170,7 +170,8 @@ def test_conv_nhwc_layout(ob, oracle, ctx):
     assert_close(y.transpose(0, 3, 1, 2), ref, 1e-5, 1e-4, "nhwc")
 
 
-def test_conv_fused_bn_residual_relu(ob, oracle, ctx):
+@pytest.mark.parametrize("precision", ["3xtf32", "fp32"])
+def test_conv_fused_bn_residual_relu(ob, oracle, ctx, precision):
     rng = np.random.default_rng(12)
     x = rng.standard_normal((2, 64, 14, 14)).astype(np.float32)
     w = (rng.standard_normal((128, 64, 3, 3)) * 0.06).astype(np.float32)
@@ -180,11 +181,11 @@ def test_conv_fused_bn_residual_relu(ob, oracle, ctx):
     mean = rng.normal(0, 0.1, 128).astype(np.float32)
     var = rng.uniform(0.5, 1.5, 128).astype(np.float32)
     res = rng.standard_normal((2, 128, 14, 14)).astype(np.float32)
-    y = run_conv(ob, ctx, x, w, b, {"pads": (1, 1, 1, 1)}, "3xtf32", relu=True,
+    y = run_conv(ob, ctx, x, w, b, {"pads": (1, 1, 1, 1)}, precision, relu=True,
                  bn=(gamma, beta, mean, var, 1e-5), residual=res)
     c = oracle.conv2d(x, w, b, (1, 1), (1, 1, 1, 1))
     ref = oracle.relu(oracle.add(oracle.batchnorm(c, gamma, beta, mean, var, 1e-5), res))
-    assert_close(y, ref, 1e-5, 1e-4, "conv+bn+add+relu")
+    assert_close(y, ref, 1e-5, 1e-4, f"conv+bn+add+relu/{precision}")
 
 
 def test_conv_tail_split_bn_residual(ob, oracle, ctx):
